@@ -1,0 +1,340 @@
+"""Benchmark of the paged-decode hot path on B200 (one JSON line on rank 0).
+
+A step is one decode step of 64 sequences on one GPU:
+  1. fused RoPE(q, k) + paged K/V append of the step's 64 new tokens
+     (32 q / 8 kv heads, head dim 128, bf16, 65536 x 16-token cache blocks),
+  2. paged-attention decode over context lengths ~ U[512, 8192]
+     (GQA 4:1, random block tables, fp32 softmax).
+`value` is decoded tokens per second summed over all ranks (weak scaling:
+each rank owns its own 64 sequences and its own KV pages, no collective on
+the data path).  The KV cache (4 GiB) is far larger than L2, so no flush is
+needed between steps.
+
+Usage:
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+  (N > 1: launch with torchrun, one rank per GPU)
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "triton-agent_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "paged-decode tokens/s"
+UNIT = "tokens/s"
+N_SEQ, HQ, HKV, D, BS, NBLK = 64, 32, 8, 128, 16, 65536
+WORKLOAD = {
+    "workload": "decode step: fused RoPE+paged KV append (64 tok) then paged-attention decode",
+    "seqs_per_gpu": N_SEQ, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "block_size": BS,
+    "num_blocks": NBLK, "context_len": "U[512,8192]", "dtype": "bf16", "rope_theta": 1e4,
+    "l2": "inputs larger than L2 (4 GiB KV cache per GPU), no flush",
+}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(ws):
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        return dist
+    return None
+
+
+def max_over_ranks(dist, v: float, device) -> float:
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"b200_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        try:
+            self.path.unlink()
+        except Exception:
+            pass
+        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs"), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# --------------------------------------------------------------------------- B200
+def run_b200(args, ws, rank, local, dist):
+    from b200ops import workloads as WL
+    from b200ops.runtime import lib as L
+    from b200ops.runtime import ops as K
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L.load()
+    seed = 1000 * rank
+    cache = WL.paged_cache(num_blocks=NBLK, block_size=BS, Hkv=HKV, D=D, device=dev, seed=seed)
+    app = WL.decode_append_inputs(cache, n_tok=N_SEQ, Hq=HQ, device=dev, seed=seed)
+    att = WL.decode_attention_inputs(cache, B=N_SEQ, Hq=HQ, device=dev, seed=seed)
+    q_out = torch.empty_like(app["q"])
+    out = torch.empty_like(att["q"])
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"], app["sin"],
+                               app["slot_mapping"], cache.k_cache, cache.v_cache, q_out=q_out)
+        K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"], out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing: per-kernel events inside the timed region
+    n = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    barrier(dist)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(n):
+            ev[i][0].record(stream)
+            K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"], app["sin"],
+                                   app["slot_mapping"], cache.k_cache, cache.v_cache, q_out=q_out)
+            ev[i][1].record(stream)
+            K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"],
+                              out=out)
+            ev[i][2].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(dist)
+    ms_local = t0.elapsed_time(t1)
+    ms = max_over_ranks(dist, ms_local, dev)
+    append_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    decode_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    clocks = clk.summary()
+    assert K.read_device_error(dev) == 0, "device error word set during the timed region"
+
+    # ---- end to end through the public API with host buffers
+    # Per-step inputs come from pinned host memory; the KV cache and the
+    # cos/sin tables are resident state (like weights) and stay on the device.
+    step_inputs = {"app_q": app["q"], "app_k": app["k"], "app_v": app["v"], "app_pos": app["positions"],
+                   "app_slots": app["slot_mapping"], "att_q": att["q"], "att_table": att["block_table"],
+                   "att_ctx": att["context_len"]}
+    pin = {k: v.cpu().pin_memory() for k, v in step_inputs.items()}
+    dev_in = {k: torch.empty_like(v, device=dev) for k, v in pin.items()}
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in pin.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for k, v in pin.items():
+            dev_in[k].copy_(v, non_blocking=True)
+        K.rope_kv_append_paged(dev_in["app_q"], dev_in["app_k"], dev_in["app_v"], dev_in["app_pos"], app["cos"],
+                               app["sin"], dev_in["app_slots"], cache.k_cache, cache.v_cache, q_out=q_out)
+        K.paged_attention(dev_in["att_q"], cache.k_cache, cache.v_cache, dev_in["att_table"], dev_in["att_ctx"],
+                          out=out)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(dist)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1), dev)
+
+    tokens = N_SEQ * ws * n
+    value = tokens / (ms / 1e3)
+    peaks = measured_peaks()
+    dec_bytes = WL.decode_bytes(att["context_len"], HQ, HKV, D, BS, index_bytes=4)
+    achieved = dec_bytes / (decode_ms / 1e3) / 1e9
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": n, "warmup": args.warmup,
+        "ms_per_step": ms / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded, on device)", "config": {**WORKLOAD, "parallelism": f"dp{ws} (sequences)"},
+        "e2e": {"value": N_SEQ * ws * n / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel", "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "peak_src": peaks["src"], "traffic": None, "algorithmic_bytes_per_launch": dec_bytes,
+                     "kernel_ms": decode_ms},
+        "per_op_ms": {"rope_kv_append_paged": append_ms, "paged_attention": decode_ms},
+        "gpu_launches": 2 * n,
+        "clocks": clocks,
+    }
+
+
+# ------------------------------------------------------------------- CPU baseline
+def cpu_decode_sample(n_seq_sample: int, seed: int = 0):
+    """Times the oracle's decode step (append rows + paged attention) on the
+    host cores for `n_seq_sample` sequences of the workload.  Returns
+    (tokens/s, seconds, sample description)."""
+    import oracle.ops as O
+
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(512, 8193, (n_seq_sample,), generator=g)
+    nb = int(((ctx + BS - 1) // BS).sum())
+    kc = torch.randn(nb, BS, HKV, D, generator=g).bfloat16()
+    vc = torch.randn(nb, BS, HKV, D, generator=g).bfloat16()
+    table = torch.randperm(nb, generator=g)
+    maxb = 8192 // BS
+    bt = torch.full((n_seq_sample, maxb), -1, dtype=torch.long)
+    off = 0
+    for b in range(n_seq_sample):
+        k = int((ctx[b] + BS - 1) // BS)
+        bt[b, :k] = table[off:off + k]
+        off += k
+    q = torch.randn(n_seq_sample, HQ, D, generator=g).bfloat16()
+    kn = torch.randn(n_seq_sample, HKV, D, generator=g).bfloat16()
+    vn = torch.randn(n_seq_sample, HKV, D, generator=g).bfloat16()
+    pos = torch.randint(0, 4096, (n_seq_sample,), generator=g)
+    cos, sin = O.rope_cos_sin(4096, D)
+    slots = torch.randperm(nb * BS, generator=g)[:n_seq_sample]
+    t0 = time.perf_counter()
+    O.rope_kv_append_paged(q, kn, vn, pos, cos, sin, slots, nb * BS)
+    O.paged_attention(q, kc, vc, bt, ctx)
+    dt = time.perf_counter() - t0
+    return n_seq_sample / dt, dt, f"{n_seq_sample} sequences of the decode step (ctx U[512,8192]), oracle port"
+
+
+def run_reference(args, ws, rank):
+    """Reference arm: the reference's CPU path (oracle port) on the host cores."""
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = 8
+    for _ in range(args.warmup):
+        cpu_decode_sample(sample, seed=1)
+    rates = []
+    t_total = 0.0
+    for i in range(args.steps):
+        r, dt, desc = cpu_decode_sample(sample, seed=2 + i)
+        rates.append(r)
+        t_total += dt
+    value = sample * args.steps / t_total
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": WORKLOAD,
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        res = run_reference(args, ws, rank)
+        if res is not None:
+            print(json.dumps(res))
+        return
+    dist = init_dist(ws)
+    try:
+        res = run_b200(args, ws, rank, local, dist)
+        if rank == 0:
+            if ws == 1 and not args.no_cpu_baseline:
+                torch.set_num_threads(os.cpu_count() or 1)
+                r, dt, desc = cpu_decode_sample(8, seed=7)
+                res["cpu_baseline"] = {"value": r, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                                       "sample": desc, "seconds": dt}
+            print(json.dumps(res))
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,224 @@
+/*
+ * b200ops.h -- C ABI of libb200ops.so, the sm_100a backend for the
+ * Triton-Agent operator library (triton_agent/ops in the reference project).
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element counts and element strides
+ *     (no torch types), plus a cudaStream_t passed as void*;
+ *   - launches asynchronously on that stream and never synchronises;
+ *   - allocates nothing: outputs and any workspace are passed in by the caller;
+ *   - returns B200_OK (0) or a negative b200_status; it never aborts or traps.
+ *
+ * Dtype codes are the b200_dtype values below.  Layouts are row-major and
+ * contiguous unless a stride argument says otherwise.
+ *
+ * Each declaration cites the reference function (file:line, paths inside the
+ * reference project) whose behaviour it reproduces.
+ */
+#ifndef B200OPS_H
+#define B200OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+typedef enum b200_status {
+  B200_OK = 0,
+  B200_ERR_BAD_ARG = -1,         /* null pointer, non-positive size, bad stride */
+  B200_ERR_UNSUPPORTED = -2,     /* dtype / shape combination not implemented */
+  B200_ERR_LAUNCH = -3,          /* cudaLaunch* or cudaFuncSetAttribute failed */
+  B200_ERR_DEVICE_TIMEOUT = -4,  /* a bounded device-side wait gave up */
+  B200_ERR_WORKSPACE = -5,       /* caller workspace missing or too small */
+  B200_ERR_NO_DEVICE = -6,       /* no sm_100 device current */
+  B200_ERR_INJECTED = -7,        /* host-side fault injection (B200OPS_INJECT_ERROR) */
+  B200_ERR_ALIGNMENT = -8        /* pointer / leading dimension not 16-byte aligned */
+} b200_status;
+
+/* ---- dtype codes ------------------------------------------------------- */
+typedef enum b200_dtype {
+  B200_F32 = 0,
+  B200_F16 = 1,
+  B200_BF16 = 2,
+  B200_I8 = 3,
+  B200_I32 = 4,
+  B200_I64 = 5
+} b200_dtype;
+
+/* ---- launch / tile parameters chosen by the tuner ----------------------
+ * A zero field means "use the kernel's default".  Each op reads only the
+ * fields it documents.  This is the CUDA-side meaning of the reference's
+ * OpAction (core/spec.py:34-61): block_d/num_warps/num_stages become
+ * threads, tiles and pipeline depth. */
+typedef struct b200_launch_cfg {
+  int32_t threads;      /* threads per CTA */
+  int32_t rows_per_cta; /* rows (tokens, sequences) handled by one CTA */
+  int32_t stages;       /* shared-memory pipeline depth */
+  int32_t split;        /* KV split (paged decode: blocks per split) / split-K */
+  int32_t tile_m;       /* GEMM / attention tile sizes */
+  int32_t tile_n;
+  int32_t tile_k;
+  int32_t flags;        /* op-specific bit flags (documented per op) */
+} b200_launch_cfg;
+
+/* ---- library info -------------------------------------------------------- */
+const char* b200_status_string(int status);
+/* Version as major*10000 + minor*100 + patch. */
+int b200_version(void);
+/* Names of the kernels compiled into this library, one per line. */
+const char* b200_kernel_list(void);
+/* Text of the last host-side failure on the calling thread (CUDA error string,
+ * injected-error note), or "" if none. */
+const char* b200_last_error_detail(void);
+/* Copies the per-library device error word (set by bounded waits that gave
+ * up, or by checked index paths) into *out and clears it.  Synchronises the
+ * given stream. */
+int b200_read_device_error(int32_t* out, void* stream);
+
+/* ---- rmsnorm ------------------------------------------------------------
+ * Replaces triton_agent/ops/rmsnorm/reference.py:6-18
+ *   y = x * rsqrt(mean(x^2, -1) + eps) * weight
+ * x, y: [rows, D] of `dtype` (F32/F16/BF16); weight: [D] of `weight_dtype`.
+ * Accumulates in fp32, rounds once to `dtype`.
+ * cfg: threads (CTA size, 64..1024). */
+int b200_rmsnorm(const void* x, const void* weight, void* y, int64_t rows,
+                 int64_t D, float eps, int32_t dtype, int32_t weight_dtype,
+                 const b200_launch_cfg* cfg, void* stream);
+
+/* ---- RoPE (NeoX rotate-half) ---------------------------------------------
+ * Replaces triton_agent/ops/rope/reference.py:6-25
+ * x, y: [B, H, T, D]; cos, sin: [T, D] of `cs_dtype` (first D/2 columns used).
+ * y1 = x1*c - x2*s ; y2 = x2*c + x1*s  (fp32, rounded once). */
+int b200_rope(const void* x, const void* cos, const void* sin, void* y,
+              int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+              int32_t cs_dtype, const b200_launch_cfg* cfg, void* stream);
+
+/* ---- contiguous KV append (in place) -------------------------------------
+ * Replaces triton_agent/ops/kv_append/reference.py:10-40
+ * k_cache, v_cache: [B, H, L, D]; k_new, v_new: [B, H, T_new, D];
+ * slot_mapping: [B, T_new] int64.  Rows whose slot is outside [0, L) are
+ * skipped.  Writes in place (the reference returns a modified clone). */
+int b200_kv_append(void* k_cache, void* v_cache, const void* k_new,
+                   const void* v_new, const int64_t* slot_mapping, int64_t B,
+                   int64_t H, int64_t L, int64_t T_new, int64_t D,
+                   int32_t dtype, const b200_launch_cfg* cfg, void* stream);
+
+/* ---- paged KV append (in place) ------------------------------------------
+ * Replaces triton_agent/ops/paged_kv/reference.py:6-27
+ * k_cache, v_cache: [num_blocks, block_size, H, D]; k_new, v_new:
+ * [B, T_new, H, D]; slot_mapping: [B, T_new] int64 global slots,
+ * block = slot / block_size, offset = slot % block_size; rows whose block is
+ * outside [0, num_blocks) are skipped. */
+int b200_paged_kv(void* k_cache, void* v_cache, const void* k_new,
+                  const void* v_new, const int64_t* slot_mapping, int64_t B,
+                  int64_t T_new, int64_t H, int64_t D, int64_t num_blocks,
+                  int64_t block_size, int32_t dtype,
+                  const b200_launch_cfg* cfg, void* stream);
+
+/* ---- RoPE + contiguous K append (in place) --------------------------------
+ * Replaces triton_agent/ops/rope_kv_append/reference.py:10-47
+ * k_new: [B, H, T_new, D]; cos, sin: [T_new, D] of `cs_dtype`;
+ * k_cache: [B, H, L, D]; slot_mapping: [B, T_new] int64. */
+int b200_rope_kv_append(const void* k_new, const void* cos, const void* sin,
+                        void* k_cache, const int64_t* slot_mapping, int64_t B,
+                        int64_t H, int64_t L, int64_t T_new, int64_t D,
+                        int32_t dtype, int32_t cs_dtype,
+                        const b200_launch_cfg* cfg, void* stream);
+
+/* ---- fused decode-step RoPE(q,k) + paged K/V append ------------------------
+ * Composition of triton_agent/ops/rope/reference.py:17-25 (rotation),
+ * rope_kv_append/reference.py:26-35 (rotate new K before writing) and
+ * paged_kv/reference.py:18-25 (slot -> block/offset, invalid skipped).
+ * q: [T, Hq, D] (may be NULL with q_out NULL); k, v: [T, Hkv, D];
+ * positions: [T] int64 row index into cos/sin tables [cs_rows, D] of
+ * `cs_dtype` (first D/2 columns used; row = position);
+ * slot_mapping: [T] int64; q_out: [T, Hq, D];
+ * k_cache, v_cache: [num_blocks, block_size, Hkv, D].
+ * K rows are written bit-exactly as round(fp32 rotation) with no FMA
+ * contraction; V rows are copied. */
+int b200_rope_kv_append_paged(const void* q, const void* k, const void* v,
+                              const int64_t* positions, const void* cos,
+                              const void* sin, int64_t cs_rows,
+                              const int64_t* slot_mapping, void* q_out,
+                              void* k_cache, void* v_cache, int64_t T,
+                              int64_t Hq, int64_t Hkv, int64_t D,
+                              int64_t num_blocks, int64_t block_size,
+                              int32_t dtype, int32_t cs_dtype,
+                              const b200_launch_cfg* cfg, void* stream);
+
+/* ---- paged attention decode -----------------------------------------------
+ * Replaces triton_agent/ops/paged_attention/reference.py:10-54 (with the
+ * query row indexed as q[b], and grouped-query attention: q head h reads kv
+ * head h / (Hq / Hkv); with Hq == Hkv this is the reference exactly).
+ * q, out: [B, Hq, D] (F16/BF16); k_cache, v_cache: [num_blocks, block_size,
+ * Hkv, D]; block_table: [B, max_blocks] of `index_dtype` (I32/I64);
+ * context_len: [B] of `index_dtype`.  Block ids outside [0, num_blocks) are
+ * skipped, as at reference.py:40-41.  scale <= 0 means 1/sqrt(D).
+ * Softmax and accumulation in fp32.  workspace: device buffer of at least
+ * b200_paged_attention_workspace_size() bytes, zero-filled once before first
+ * use (the kernel leaves it ready for the next call).
+ * cfg: split (KV blocks per split, default 32), stages (default 3). */
+size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq,
+                                           int64_t max_blocks,
+                                           int64_t block_size, int64_t D,
+                                           const b200_launch_cfg* cfg);
+int b200_paged_attention(const void* q, const void* k_cache,
+                         const void* v_cache, const void* block_table,
+                         const void* context_len, void* out, int64_t B,
+                         int64_t Hq, int64_t Hkv, int64_t D,
+                         int64_t num_blocks, int64_t block_size,
+                         int64_t max_blocks, float scale, int32_t dtype,
+                         int32_t index_dtype, void* workspace,
+                         size_t workspace_bytes, const b200_launch_cfg* cfg,
+                         void* stream);
+
+/* ---- INT8 GEMM with fused dequant epilogue --------------------------------
+ * Restates triton_agent/ops/quant_matmul/reference.py:26-27 for
+ * pre-quantised operands:
+ *   acc[m,n] = sum_k A[m,k] * W[n,k]            (int8 x int8 -> int32, exact)
+ *   C[m,n]   = out_dtype( float(acc) * sA[m] * sW[n] )
+ * A: [M, K] int8 row-major; W: [N, K] int8 row-major (K-major); sA: [M] f32;
+ * sW: [N] f32; C: [M, N] with row stride ldc (elements) of `out_dtype`
+ * (F16/BF16/F32).  acc_out (nullable): [M, N] int32 raw accumulators.
+ * K must be a multiple of 16 and A/W 16-byte aligned.
+ * workspace: needed only for split-K (small M); size from
+ * b200_int8_gemm_workspace_size().  cfg: tile_n, stages, split. */
+size_t b200_int8_gemm_workspace_size(int64_t M, int64_t N, int64_t K,
+                                     const b200_launch_cfg* cfg);
+int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
+                   const float* sW, void* C, int64_t M, int64_t N, int64_t K,
+                   int64_t ldc, int32_t out_dtype, int32_t* acc_out,
+                   void* workspace, size_t workspace_bytes,
+                   const b200_launch_cfg* cfg, void* stream);
+
+/* ---- symmetric INT8 quantisation -------------------------------------------
+ * Restates triton_agent/ops/quant_matmul/reference.py:16-24:
+ *   scale = max|x| / 127 (0 -> 1e-6), q = clamp(round_half_even(x / scale), -127, 127)
+ * Row mode (`by_column` = 0): x [rows, cols] -> q [rows, cols], scale [rows].
+ * Column mode (`by_column` = 1): x [rows, cols] (e.g. b [K, N]) is quantised
+ * per column and written transposed: q [cols, rows], scale [cols].
+ * scale_dtype is the dtype the reference's scale tensor has (that of x);
+ * the division uses the scale rounded to that dtype, as the reference does. */
+int b200_quantize_int8(const void* x, int8_t* q, float* scale, int64_t rows,
+                       int64_t cols, int32_t dtype, int32_t by_column,
+                       const b200_launch_cfg* cfg, void* stream);
+
+/* ---- causal / full flash attention prefill -----------------------------------
+ * Replaces triton_agent/ops/flash_attn_like/reference.py:7-31
+ * q: [B, H, T, D]; k, v: [B, H, S, D]; o: [B, H, T, D]; dtype F16/BF16;
+ * D = 128 on the tensor-core path.  causal: mask key s > query t
+ * (reference.py:25-28, which assumes T == S).  lse (nullable): [B, H, T] f32
+ * natural-log softmax normaliser.  scale <= 0 means 1/sqrt(D). */
+int b200_flash_attn(const void* q, const void* k, const void* v, void* o,
+                    float* lse, int64_t B, int64_t H, int64_t T, int64_t S,
+                    int64_t D, float scale, int32_t causal, int32_t dtype,
+                    const b200_launch_cfg* cfg, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200OPS_H */

@@ -1,0 +1,79 @@
+"""GPU parity: tcgen05 INT8 GEMM.  int32 accumulators are bit-exact against
+the oracle's exact integer GEMM; the dequantised output is bit-exact too
+(same fp32 product order, one final rounding); the reference-API path
+(quantise a and b, GEMM, rescale) matches the reference's fp32 output."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.ops as O
+from b200ops import workloads as WL
+from b200ops.runtime import ops as K
+
+pytestmark = pytest.mark.gpu
+
+
+def check(M, N, K_, cuda_device, out_dtype=torch.float16, cfg=None, seed=0):
+    A, W, sA, sW = WL.int8_gemm_inputs(M, N, K_, device=cuda_device, seed=seed)
+    acc = torch.empty(M, N, dtype=torch.int32, device=cuda_device)
+    C = K.int8_gemm(A, W, sA, sW, out_dtype=out_dtype, acc_out=acc, cfg=cfg)
+    torch.cuda.synchronize()
+    assert K.read_device_error() == 0
+    exp_acc = O.int8_gemm_acc(A.cpu(), W.cpu())
+    assert np.array_equal(acc.cpu().numpy().astype(np.int64), exp_acc)
+    exp = O.dequant(exp_acc, sA.cpu(), sW.cpu(), out_dtype)
+    assert torch.equal(C.cpu(), exp)
+
+
+@pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (256, 512, 1024), (130, 200, 48), (1, 8, 16),
+                                    (300, 1000, 4096), (16, 4096, 4096)])
+def test_int8_gemm_exact(M, N, K_, cuda_device):
+    check(M, N, K_, cuda_device)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_int8_gemm_out_dtypes(out_dtype, cuda_device):
+    check(200, 384, 512, cuda_device, out_dtype=out_dtype)
+
+
+@pytest.mark.parametrize("cfg", [{"tile_n": 128}, {"tile_n": 256}, {"split": 4}, {"stages": 2},
+                                 {"tile_n": 128, "split": 3, "stages": 3}])
+def test_int8_gemm_configs(cfg, cuda_device):
+    check(256, 768, 2048, cuda_device, cfg=cfg)
+
+
+def test_int8_gemm_baseline_shapes_checksum(cuda_device):
+    """Full BASELINE shapes: exact integer checks that do not need a full
+    CPU GEMM -- column sums of the accumulator equal (1^T A) W^T and row sums
+    equal A (W^T 1), both in int64, plus a sampled block compared exactly."""
+    for M, N in [(4096, 4096), (4096, 14336), (16, 14336)]:
+        K_ = 4096
+        A, W, sA, sW = WL.int8_gemm_inputs(M, N, K_, device=cuda_device)
+        acc = torch.empty(M, N, dtype=torch.int32, device=cuda_device)
+        C = K.int8_gemm(A, W, sA, sW, acc_out=acc)
+        col = acc.to(torch.int64).sum(0).cpu()
+        row = acc.to(torch.int64).sum(1).cpu()
+        a64 = A.cpu().numpy().astype(np.int64)
+        w64 = W.cpu().numpy().astype(np.int64)
+        assert np.array_equal(col.numpy(), a64.sum(0) @ w64.T)
+        assert np.array_equal(row.numpy(), a64 @ w64.sum(0))
+        r0, c0 = M // 3, N // 5
+        blk = O.int8_gemm_acc(A[r0:r0 + 16].cpu(), W[c0:c0 + 64].cpu())
+        assert np.array_equal(acc[r0:r0 + 16, c0:c0 + 64].cpu().numpy().astype(np.int64), blk)
+        exp = O.dequant(blk, sA[r0:r0 + 16].cpu(), sW[c0:c0 + 64].cpu(), torch.float16)
+        assert torch.equal(C[r0:r0 + 16, c0:c0 + 64].cpu(), exp)
+
+
+def test_quant_matmul_reference_api_golden(golden_dir, cuda_device):
+    """quantise a per row and b per column on the GPU, int8 GEMM, fp32
+    rescale -- equals the reference's quant_matmul output bit for bit."""
+    for c in torch.load(golden_dir / "quant_matmul.pt"):
+        a, b = c["a"].to(cuda_device), c["b"].to(cuda_device)
+        lead, (M, K_) = a.shape[:-2], a.shape[-2:]
+        qa, sa = K.quantize_int8(a.reshape(-1, K_))
+        qb, sb = K.quantize_int8(b, by_column=True)
+        if K_ % 16:
+            pytest.skip("K not a multiple of 16")
+        out = K.int8_gemm(qa, qb, sa, sb, out_dtype=torch.float32).reshape(*lead, M, -1)
+        assert torch.equal(out.cpu(), c["c"])

@@ -1,0 +1,482 @@
+// Flash attention forward (prefill), bf16/fp16, fp32 softmax statistics, on
+// the 5th-generation tensor cores (tcgen05.mma kind::f16, accumulators in
+// tensor memory).
+//
+// Reference: triton_agent/ops/flash_attn_like/reference.py:22-31
+//   scores = q k^T / sqrt(D); causal: key s > query t masked (tril mask);
+//   out = softmax(scores) v
+//
+// One CTA per (128 query rows, b*h).  Warp roles (192 threads):
+//   warp 0      TMA producer: Q tile once; K and V tiles of 128 keys into a
+//               2-stage ring (3-D tensor maps [B*H, T, D], SWIZZLE_128B,
+//               boxes of 64 head dims, so every row / key past the end of a
+//               head reads zeros instead of the next head)
+//   warp 1      allocates 512 TMEM columns (S double buffer 2x128, O 128 or
+//               64); one lane issues S_j = Q K_j^T (kind::f16, M=128, N=128,
+//               K=16 steps) ahead of the softmax, then O += P_j V_j with P
+//               from shared memory (K-major) and V as an MN-major operand
+//   warps 2..5  softmax: each thread owns one query row (TMEM lane), loads
+//               its 128 scores, masks (causal diagonal / key tail), keeps a
+//               running max that is only raised when it grows by more than
+//               2^8 (then O is rescaled in TMEM), writes P = exp2(s - m) as
+//               bf16 into a SWIZZLE_128B K-major tile, and finally divides O
+//               by the row sum and stores the output row.
+// The running-max rule is exact: O and l share the same offset, which
+// cancels in O / l; it only bounds P <= 2^8.  Causal CTAs are launched
+// heaviest-first (last query tiles first) to shorten the tail.  No cluster
+// multicast is used.
+#include <math.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+B200_DEVICE_ERROR_WORD()
+
+namespace b200 {
+namespace {
+
+constexpr int kBM = 128;   // query rows per CTA
+constexpr int kBN = 128;   // keys per tile
+constexpr int kThreads = 192;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FlashParams {
+  int64_t B, H, T, S;
+  int n_qt;         // query tiles
+  float sl2;        // scale * log2(e)
+  int causal;
+  int out_lse;
+};
+
+template <int D>
+struct FlashSmem {
+  static constexpr uint32_t kHalf = kBM * 128;          // one 64-dim box: 128 rows x 128 B
+  static constexpr uint32_t kQ = (D / 64) * kHalf;       // Q tile
+  static constexpr uint32_t kKV = (D / 64) * kHalf;      // K or V tile (128 keys)
+  static constexpr uint32_t kP = 2 * kHalf;              // P tile 128 x 128 bf16
+  static constexpr uint32_t oQ = 0;
+  static constexpr uint32_t oK0 = oQ + kQ;
+  static constexpr uint32_t oV0 = oK0 + kKV;
+  static constexpr uint32_t oK1 = oV0 + kKV;
+  static constexpr uint32_t oV1 = oK1 + kKV;
+  static constexpr uint32_t oP = oV1 + kKV;
+  static constexpr uint32_t oBar = oP + kP;
+  static constexpr uint32_t kTotal = oBar + 256 + 1024;  // + barriers + alignment slack
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
+                             float* __restrict__ lse, FlashParams p) {
+  using L = FlashSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = sm100::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int qt = p.n_qt - 1 - (int)blockIdx.y;  // heaviest query tiles first
+  const int64_t q0 = (int64_t)qt * kBM;
+  const int n_kt_all = (int)((p.S + kBN - 1) / kBN);
+  const int n_kt = p.causal ? min(n_kt_all, (int)((q0 + kBM + kBN - 1) / kBN)) : n_kt_all;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* v_full = bars + 3;     // [2]
+  uint64_t* kv_empty = bars + 5;   // [2]
+  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(sm100::smem_u32(q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(sm100::smem_u32(&k_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&v_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&kv_empty[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&s_full[i]), 1);
+    }
+    sm100::mbar_init(sm100::smem_u32(p_full), 4);
+    sm100::mbar_init(sm100::smem_u32(o_done), 1);
+    *s_abort = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(sm100::smem_u32(tmem_slot), 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_q);
+      sm100::tma_prefetch_desc(&tm_k);
+      sm100::tma_prefetch_desc(&tm_v);
+      const uint32_t qb = sm100::smem_u32(q_full);
+      sm100::mbar_arrive_expect_tx(qb, L::kQ);
+#pragma unroll
+      for (int h = 0; h < D / 64; ++h)
+        sm100::tma_load_3d(sbase + L::oQ + h * L::kHalf, &tm_q, qb, h * 64, (int32_t)q0, bh);
+      int issued = 0;
+      for (int j = 0; j < n_kt; ++j) {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&kv_empty[s]), ((j >> 1) & 1) ^ 1)) {
+          b200_dev_error(kDevErrTimeoutEmpty);
+          atomicExch(s_abort, 1);
+          break;
+        }
+        if (*(volatile int*)s_abort) break;
+        const uint32_t kb = sm100::smem_u32(&k_full[s]);
+        const uint32_t vb = sm100::smem_u32(&v_full[s]);
+        const uint32_t ko = s ? L::oK1 : L::oK0;
+        const uint32_t vo = s ? L::oV1 : L::oV0;
+        sm100::mbar_arrive_expect_tx(kb, L::kKV);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + ko + h * L::kHalf, &tm_k, kb, h * 64, j * kBN, bh);
+        sm100::mbar_arrive_expect_tx(vb, L::kKV);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + vo + h * L::kHalf, &tm_v, vb, h * 64, j * kBN, bh);
+        ++issued;
+      }
+      // drain: never exit with bulk copies landing in shared memory
+      if (!sm100::mbar_wait(sm100::smem_u32(q_full), 0)) b200_dev_error(kDevErrTimeoutFull);
+      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j) {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&k_full[s]), (j >> 1) & 1)) b200_dev_error(kDevErrTimeoutFull);
+        if (!sm100::mbar_wait(sm100::smem_u32(&v_full[s]), (j >> 1) & 1)) b200_dev_error(kDevErrTimeoutFull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_s = sm100::make_idesc(1, fmt, fmt, 0, 0, kBM, kBN);
+      constexpr uint32_t idesc_o = sm100::make_idesc(1, fmt, fmt, 0, 1, kBM, D);
+      bool ok = sm100::mbar_wait(sm100::smem_u32(q_full), 0);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&k_full[s]), (j >> 1) & 1)) return false;
+        sm100::tc_fence_after();
+        const uint32_t kbase = sbase + (s ? L::oK1 : L::oK0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kHalf + (kk & 3) * 32;
+          const uint64_t ad = sm100::make_smem_desc(sbase + L::oQ + off, 16, 1024, sm100::kSwizzle128B);
+          const uint64_t bd = sm100::make_smem_desc(kbase + off, 16, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ss(tS[s], ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        sm100::tc_commit(sm100::smem_u32(&s_full[s]));
+        return true;
+      };
+      if (ok && n_kt > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kt; ++j) {
+        const int s = j & 1;
+        if (*(volatile int*)s_abort) {
+          ok = false;
+          break;
+        }
+        if (j + 1 < n_kt && !(ok = issue_s(j + 1))) break;
+        if (!sm100::mbar_wait(sm100::smem_u32(p_full), j & 1) ||
+            !sm100::mbar_wait(sm100::smem_u32(&v_full[s]), (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t vbase = sbase + (s ? L::oV1 : L::oV0);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // P: K-major, keys 64*(kk/4).. in box kk/4, 32-byte step inside it.
+          const uint64_t ad = sm100::make_smem_desc(sbase + L::oP + (kk >> 2) * L::kHalf + (kk & 3) * 32, 16,
+                                                    1024, sm100::kSwizzle128B);
+          // V: MN-major; 16 keys = two 8-row groups of 128 B (SBO 1024),
+          // head-dim halves 64 apart live one box (16 KB) apart (LBO).
+          const uint64_t bd = sm100::make_smem_desc(vbase + kk * 2048, L::kHalf, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ss(tO, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        sm100::tc_commit(sm100::smem_u32(o_done));
+        sm100::tc_commit(sm100::smem_u32(&kv_empty[s]));
+      }
+      if (!ok) {
+        b200_dev_error(kDevErrTimeoutFull);
+        atomicExch(s_abort, 1);
+        // all issued MMAs must finish before TMEM is released
+        sm100::tc_commit(sm100::smem_u32(o_done));
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;          // row inside the tile = TMEM lane
+    const int64_t qrow = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      const int s = j & 1;
+      if (!sm100::mbar_wait(sm100::smem_u32(&s_full[s]), (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      uint32_t sr[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) sm100::tmem_ld_32x32b_x32(tS[s] + lane_off + c * 32, sr + c * 32);
+      sm100::tmem_wait_ld();
+      const int64_t k0 = (int64_t)j * kBN;
+      const bool need_mask = (k0 + kBN > p.S) || (p.causal && k0 + kBN - 1 > qrow);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        float x = __uint_as_float(sr[c]) * p.sl2;
+        if (need_mask) {
+          const int64_t key = k0 + c;
+          if (key >= p.S || (p.causal && key > qrow)) x = -INFINITY;
+        }
+        sr[c] = __float_as_uint(x);
+        mx = fmaxf(mx, x);
+      }
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m_used == -INFINITY) {
+        m_used = mx;
+      } else if (mx > m_used + kRescaleThreshold) {
+        alpha = exp2f(m_used - mx);
+        m_used = mx;
+        rescale = true;
+      }
+      float sum = 0.f;
+      uint32_t pk[kBN / 2];
+#pragma unroll
+      for (int c = 0; c < kBN; c += 2) {
+        const float p0 = exp2f(__uint_as_float(sr[c]) - m_used);
+        const float p1 = exp2f(__uint_as_float(sr[c + 1]) - m_used);
+        sum += p0 + p1;
+        pk[c / 2] = pack2<T>(p0, p1);
+      }
+      l = l * alpha + sum;
+      // PV_{j-1} must be complete before P is overwritten or O is rescaled.
+      if (j > 0 && !sm100::mbar_wait(sm100::smem_u32(o_done), (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        sm100::tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          sm100::tmem_ld_32x32b_x32(tO + lane_off + c, o);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          sm100::tmem_st_32x32b_x16(tO + lane_off + c, o);
+          sm100::tmem_st_32x32b_x16(tO + lane_off + c + 16, o + 16);
+        }
+        sm100::tmem_wait_st();
+      }
+      // P row r -> K-major SWIZZLE_128B tile: keys [64h, 64h+64) in box h,
+      // row r at (r/8)*1024 + (r%8)*128, 16-byte chunk c at (c ^ (r%8))*16.
+      const uint32_t prow = sbase + L::oP + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t* v = pk + h * 32 + c * 4;
+          sts128(prow + h * L::kHalf + ((c ^ (r & 7)) << 4), v[0], v[1], v[2], v[3]);
+        }
+      sm100::fence_proxy_async_smem();  // generic-proxy P stores -> tensor-core reads
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(p_full));
+    }
+    // epilogue
+    if (ok && n_kt > 0 && !sm100::mbar_wait(sm100::smem_u32(o_done), (n_kt - 1) & 1)) ok = false;
+    if (!ok) {
+      b200_dev_error(kDevErrTimeoutMma);
+      atomicExch(s_abort, 1);
+    }
+    sm100::tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const bool row_ok = qrow < p.T;
+    T* orow = out + ((int64_t)bh * p.T + qrow) * D;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t o[32];
+      sm100::tmem_ld_32x32b_x32(tO + lane_off + c, o);
+      sm100::tmem_wait_ld();
+      if (row_ok && ok) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c + 8 * v) = w;
+        }
+      }
+    }
+    if (p.out_lse && row_ok) lse[(int64_t)bh * p.T + qrow] = (m_used + log2f(l)) * 0.6931471805599453f;
+    sm100::tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// General fallback for head dims the tensor-core path does not cover (<= 256):
+// one warp per query row, lanes over keys, fp32 online softmax.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) flash_generic_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                            const T* __restrict__ v, T* __restrict__ out,
+                                                            float* __restrict__ lse, FlashParams p, int D) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;  // flattened (bh, t)
+  if (row >= p.B * p.H * p.T) return;
+  const int64_t bh = row / p.T, t = row % p.T;
+  const T* qr = q + row * D;
+  const T* kb = k + bh * p.S * D;
+  const T* vb = v + bh * p.S * D;
+  float acc[8];
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const int64_t s_end = p.causal ? min(p.S, t + 1) : p.S;
+  for (int64_t s0 = 0; s0 < s_end; s0 += 32) {
+    const int64_t s = s0 + lane;
+    float x = -INFINITY;
+    if (s < s_end) {
+      float d = 0.f;
+      for (int i = 0; i < D; ++i) d = fmaf(to_f32(qr[i]), to_f32(kb[s * D + i]), d);
+      x = d * p.sl2;
+    }
+    const float mx = warp_max(x);
+    const float mn = fmaxf(m, mx);
+    const float a = (m == -INFINITY) ? 0.f : exp2f(m - mn);
+    const float pw = (x == -INFINITY) ? 0.f : exp2f(x - mn);
+    l = l * a + warp_sum(pw);
+    for (int i = 0; i < 8; ++i) acc[i] *= a;
+    for (int j = 0; j < 32; ++j) {
+      const float pj = __shfl_sync(0xffffffffu, pw, j);
+      const int64_t sj = s0 + j;
+      if (sj >= s_end) break;
+      for (int i = 0; i < 8; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) acc[i] = fmaf(pj, to_f32(vb[sj * D + d]), acc[i]);
+      }
+    }
+    m = mn;
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < D) out[row * D + d] = from_f32<T>(acc[i] * inv);
+  }
+  if (p.out_lse && lane == 0) lse[row] = (m + log2f(l)) * 0.6931471805599453f;
+}
+
+template <typename T, int D>
+int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, const FlashParams& p,
+              cudaStream_t s) {
+  const CUtensorMapDataType dt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[3] = {64, 128, 1};
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)p.T, (uint64_t)(p.B * p.H)};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)p.T * D * 2};
+    int st = encode_tensor_map(&tq, dt, 3, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)p.S, (uint64_t)(p.B * p.H)};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)p.S * D * 2};
+    int st = encode_tensor_map(&tk, dt, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_tensor_map(&tv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
+  auto kern = flash_fwd_tcgen05_kernel<T, D>;
+  const int smem = (int)FlashSmem<D>::kTotal;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return launch_status(e);
+  dim3 grid((unsigned)(p.B * p.H), (unsigned)p.n_qt);
+  kern<<<grid, kThreads, smem, s>>>(tq, tk, tv, static_cast<T*>(o), lse, p);
+  return launch_status(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
+                               int64_t H, int64_t T, int64_t S, int64_t D, float scale, int32_t causal,
+                               int32_t dtype, const b200_launch_cfg* cfg, void* stream) {
+  (void)cfg;
+  if (int e = injected_error("flash_attn")) return e;
+  if (B < 0 || H < 0 || T < 0 || S < 0 || D <= 0) return B200_ERR_BAD_ARG;
+  if (causal && T != S) return B200_ERR_BAD_ARG;  // the reference's tril mask assumes T == S
+  if (B * H * T == 0) return B200_OK;
+  if (!q || !k || !v || !o) return B200_ERR_BAD_ARG;
+  if (S == 0) return B200_ERR_BAD_ARG;
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+  FlashParams p;
+  p.B = B;
+  p.H = H;
+  p.T = T;
+  p.S = S;
+  p.n_qt = (int)((T + kBM - 1) / kBM);
+  p.sl2 = scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.out_lse = lse != nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool tc = (D == 64 || D == 128) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) &&
+                  B * H <= 0x7fffffffLL && p.n_qt <= 65535 && T < (1ll << 31) && S < (1ll << 31);
+  if (tc) {
+    return B200_DISPATCH_HALF(dtype, [&] {
+      return D == 128 ? launch_tc<scalar_t, 128>(q, k, v, o, lse, p, s)
+                      : launch_tc<scalar_t, 64>(q, k, v, o, lse, p, s);
+    });
+  }
+  if (D > 256) return B200_ERR_UNSUPPORTED;
+  return B200_DISPATCH_HALF(dtype, [&] {
+    const int64_t rows = B * H * T;
+    flash_generic_kernel<scalar_t><<<(unsigned)((rows + 3) / 4), 128, 0, s>>>(
+        static_cast<const scalar_t*>(q), static_cast<const scalar_t*>(k), static_cast<const scalar_t*>(v),
+        static_cast<scalar_t*>(o), lse, p, (int)D);
+    return launch_status(cudaGetLastError());
+  });
+}

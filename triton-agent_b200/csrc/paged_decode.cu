@@ -1,0 +1,654 @@
+// Paged-attention decode (one query token per sequence), grouped-query.
+//
+// Reference: triton_agent/ops/paged_attention/reference.py:26-52.  For each
+// sequence b the reference walks the first ceil(ctx/block_size) entries of
+// block_table[b], drops ids outside [0, num_blocks) (reference.py:40-41),
+// concatenates the remaining blocks' tokens, truncates to ctx tokens
+// (reference.py:47-48) and computes softmax(q . K^T * scale) . V in fp32.
+// Consequently the j-th *valid* block (rank j among valid ones) supplies
+// tokens [j*bs, j*bs + bs) of the concatenation, of which
+// clamp(ctx - j*bs, 0, bs) survive the truncation; this kernel reproduces
+// that rule exactly.  Query head h reads kv head h / (Hq / Hkv).
+//
+// Structure (HBM-bound; algorithmic bytes = 2 * ctx * Hkv * D * 2 per
+// sequence for K and V, plus q, out and the block table):
+//   grid  = (splits, B, Hkv / HG), one CTA per (split, sequence, head group)
+//   warps = HG consumer warps (one per kv head) + 1 producer warp
+//   The producer warp builds the split's page list from the block table,
+//   then one lane streams whole pages -- K and V tiles [bs][HG][D] of all
+//   HG heads -- into a ring of shared-memory stages with 3-D TMA loads
+//   (mbarrier complete_tx).  Consumer warp w owns kv head h0 + w and its G
+//   query heads: 8 lanes per token (16 of the 128 dims each), 4 tokens in
+//   flight per warp, q.k reduced with 3 xor-shuffles, fp32 online softmax
+//   in base 2, P.V accumulated in registers.  Lane groups merge at the end.
+//   When a sequence spans several splits, each CTA writes (m, l, o) to the
+//   workspace and the last CTA to finish (atomic ticket) merges them and
+//   resets the ticket, so one launch does the whole op.
+#include <math.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+B200_DEVICE_ERROR_WORD()
+
+namespace b200 {
+namespace {
+
+constexpr int kD = 128;           // head dim of the TMA path
+constexpr int kMaxSplitBlocks = 256;
+constexpr int kMaxSplits = 1024;
+constexpr size_t kTicketBytes = 256 * 1024;  // one int per (sequence, head group), <= 65536
+
+struct DecodeParams {
+  int64_t B, Hq, Hkv, num_blocks, block_size, max_blocks;
+  int HG;            // kv heads per CTA (= consumer warps)
+  int n_hg;          // Hkv / HG
+  int split_blocks;  // block-table entries per split
+  int max_splits;    // ceil(max_blocks / split_blocks)
+  int stages;
+  uint32_t stage_bytes;  // K + V tile bytes of one page
+  uint32_t tiles_bytes;  // bytes before the barriers (stage ring, or combine weights if larger)
+  float qscale;          // scale * log2(e)
+};
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void widen8(const uint4& raw, float* f) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+    unpack16<T>(raw, f);
+  }
+}
+
+template <typename IDX>
+__device__ __forceinline__ bool bad_block(IDX id, int64_t nb) {
+  return id < 0 || (int64_t)id >= nb;
+}
+
+template <typename T, typename IDX, int G>
+__global__ void __launch_bounds__(288, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const T* __restrict__ q,
+                        const IDX* __restrict__ block_table, const IDX* __restrict__ ctx_len,
+                        T* __restrict__ out, float* __restrict__ ws_o, float* __restrict__ ws_ml,
+                        int* __restrict__ tickets, DecodeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int64_t b = blockIdx.y;
+  const int hg = blockIdx.z;
+  const int HG = p.HG;
+  const int heads_cta = HG * G;
+  const int64_t bs = p.block_size;
+
+  // Shared-memory carve-up: [stages x (K tile | V tile)] [bars] [page list] [scalars]
+  const uint32_t tiles_bytes = p.tiles_bytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + tiles_bytes);
+  uint64_t* empty_bar = full_bar + p.stages;
+  int* list_id = reinterpret_cast<int*>(empty_bar + p.stages);
+  int* list_ntok = list_id + kMaxSplitBlocks;
+  int* s_misc = list_ntok + kMaxSplitBlocks;  // [0] npages, [1] abort, [2] last-CTA flag
+  float* s_wts = reinterpret_cast<float*>(smem);  // combine weights, reuses the tiles
+
+  int64_t ctx = (int64_t)ctx_len[b];
+  const int64_t nvb64 = ctx > 0 ? (ctx + bs - 1) / bs : 0;
+  const int nvb = (int)(nvb64 < p.max_blocks ? nvb64 : p.max_blocks);
+  const int nsplit = (nvb + p.split_blocks - 1) / p.split_blocks;
+  const int64_t out_row0 = b * p.Hq + (int64_t)hg * heads_cta;
+
+  if (nvb == 0) {
+    // No context: the output rows are zero (the reference has nothing to
+    // concatenate here and fails; zero is this library's defined result).
+    if (split == 0) {
+      for (int i = threadIdx.x; i < heads_cta * kD; i += blockDim.x)
+        out[out_row0 * kD + i] = from_f32<T>(0.f);
+    }
+    return;
+  }
+  if (split >= nsplit) return;
+  const int p0 = split * p.split_blocks;
+  const int p1 = min(p0 + p.split_blocks, nvb);
+  const IDX* bt = block_table + b * p.max_blocks;
+
+  // ---- page list: valid blocks of this split with their surviving tokens
+  if (warp == HG) {
+    int inval = 0;
+    for (int j = lane; j < p0; j += 32) inval += bad_block(bt[j], p.num_blocks) ? 1 : 0;
+    inval = __reduce_add_sync(0xffffffffu, inval);
+    int count = 0;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int j0 = p0; j0 < p1; j0 += 32) {
+      const int j = j0 + lane;
+      const bool in = j < p1;
+      const IDX id = in ? bt[j] : (IDX)-1;
+      const bool valid = in && !bad_block(id, p.num_blocks);
+      const unsigned ib = __ballot_sync(0xffffffffu, in && !valid);
+      const int64_t rank = (int64_t)j - (inval + __popc(ib & lt_mask));
+      int64_t nt = ctx - rank * bs;
+      nt = nt < 0 ? 0 : (nt > bs ? bs : nt);
+      const bool use = valid && nt > 0;
+      const unsigned ub = __ballot_sync(0xffffffffu, use);
+      if (use) {
+        const int slot = count + __popc(ub & lt_mask);
+        list_id[slot] = (int)id;
+        list_ntok[slot] = (int)nt;
+      }
+      count += __popc(ub);
+      inval += __popc(ib);
+    }
+    if (lane == 0) {
+      s_misc[0] = count;
+      s_misc[1] = 0;
+      for (int s = 0; s < p.stages; ++s) {
+        sm100::mbar_init(sm100::smem_u32(&full_bar[s]), 1);
+        sm100::mbar_init(sm100::smem_u32(&empty_bar[s]), HG);
+      }
+      sm100::fence_barrier_init();
+    }
+  }
+  __syncthreads();
+  const int npages = s_misc[0];
+
+  // Per-lane online-softmax state (consumers only).
+  float m[G], l[G], o[G][16];
+  const int grp = lane >> 3, sub = lane & 7;
+
+  if (warp == HG) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_k);
+      sm100::tma_prefetch_desc(&tm_v);
+      const uint32_t base = sm100::smem_u32(smem);
+      int issued = 0;
+      for (int i = 0; i < npages; ++i) {
+        const int s = i % p.stages;
+        const uint32_t parity = ((i / p.stages) & 1) ^ 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&empty_bar[s]), parity)) {
+          b200_dev_error(kDevErrTimeoutEmpty);
+          atomicExch(&s_misc[1], 1);
+          break;
+        }
+        if (*(volatile int*)&s_misc[1]) break;
+        const uint32_t fb = sm100::smem_u32(&full_bar[s]);
+        sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
+        const int32_t tok0 = list_id[i] * (int32_t)bs;
+        const uint32_t dst = base + s * p.stage_bytes;
+        sm100::tma_load_3d(dst, &tm_k, fb, 0, hg * HG, tok0);
+        sm100::tma_load_3d(dst + p.stage_bytes / 2, &tm_v, fb, 0, hg * HG, tok0);
+        ++issued;
+      }
+      // Never leave the CTA with bulk copies still landing in shared memory:
+      // wait (bounded) for the last fill of every stage.
+      for (int i = issued - 1; i >= 0 && i >= issued - p.stages; --i) {
+        const int s = i % p.stages;
+        if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1))
+          b200_dev_error(kDevErrTimeoutFull);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- consumers
+    const int w = warp;
+    const int64_t kvh = (int64_t)hg * HG + w;
+    float qf[G][16];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const T* qr = q + (b * p.Hq + kvh * G + g) * kD;
+      float f[8];
+      load16_f32(qr + 8 * sub, f);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) qf[g][d] = f[d] * p.qscale;
+      load16_f32(qr + 64 + 8 * sub, f);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) qf[g][8 + d] = f[d] * p.qscale;
+      m[g] = -INFINITY;
+      l[g] = 0.f;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) o[g][d] = 0.f;
+    }
+    const uint32_t base = sm100::smem_u32(smem);
+    const uint32_t row_bytes = kD * 2;
+    const uint32_t tok_bytes = HG * row_bytes;
+    const uint32_t lane_off = w * row_bytes + sub * 16;
+
+    for (int i = 0; i < npages; ++i) {
+      const int s = i % p.stages;
+      if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+        b200_dev_error(kDevErrTimeoutFull);
+        atomicExch(&s_misc[1], 1);
+        break;
+      }
+      if (*(volatile int*)&s_misc[1]) break;
+      const int ntok = list_ntok[i];
+      const uint32_t kb = base + s * p.stage_bytes + lane_off;
+      const uint32_t vb = kb + p.stage_bytes / 2;
+      for (int t0 = 0; t0 < ntok; t0 += 16) {
+        float sc[4][G];
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+          const int tok = t0 + 4 * pp + grp;
+          const bool ok = tok < ntok;
+          float part[G];
+#pragma unroll
+          for (int g = 0; g < G; ++g) part[g] = 0.f;
+          if (ok) {
+            float kf[16];
+            widen8<T>(lds128(kb + tok * tok_bytes), kf);
+            widen8<T>(lds128(kb + tok * tok_bytes + 128), kf + 8);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+              for (int d = 0; d < 8; ++d) {
+                a0 = fmaf(qf[g][d], kf[d], a0);
+                a1 = fmaf(qf[g][8 + d], kf[8 + d], a1);
+              }
+              part[g] = a0 + a1;
+            }
+          }
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            part[g] += __shfl_xor_sync(0xffffffffu, part[g], 1);
+            part[g] += __shfl_xor_sync(0xffffffffu, part[g], 2);
+            part[g] += __shfl_xor_sync(0xffffffffu, part[g], 4);
+            sc[pp][g] = ok ? part[g] : -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float mx = fmaxf(fmaxf(sc[0][g], sc[1][g]), fmaxf(sc[2][g], sc[3][g]));
+          const float mnew = fmaxf(m[g], mx);
+          const float alpha = (m[g] == mnew) ? 1.f : exp2f(m[g] - mnew);
+          m[g] = mnew;
+          float psum = 0.f;
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) {
+            sc[pp][g] = (sc[pp][g] == -INFINITY) ? 0.f : exp2f(sc[pp][g] - mnew);
+            psum += sc[pp][g];
+          }
+          l[g] = fmaf(l[g], alpha, psum);
+#pragma unroll
+          for (int d = 0; d < 16; ++d) o[g][d] *= alpha;
+        }
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+          const int tok = t0 + 4 * pp + grp;
+          if (tok < ntok) {
+            float vf[16];
+            widen8<T>(lds128(vb + tok * tok_bytes), vf);
+            widen8<T>(lds128(vb + tok * tok_bytes + 128), vf + 8);
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+              for (int d = 0; d < 16; ++d) o[g][d] = fmaf(sc[pp][g], vf[d], o[g][d]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&empty_bar[s]));
+    }
+
+    // Merge the four lane groups (tokens were dealt round-robin to them).
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int x = 8; x <= 16; x <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m[g], x);
+        const float lo = __shfl_xor_sync(0xffffffffu, l[g], x);
+        const float mn = fmaxf(m[g], mo);
+        const float a = (m[g] == -INFINITY) ? 0.f : exp2f(m[g] - mn);
+        const float c = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+        l[g] = l[g] * a + lo * c;
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+          const float oo = __shfl_xor_sync(0xffffffffu, o[g][d], x);
+          o[g][d] = o[g][d] * a + oo * c;
+        }
+        m[g] = mn;
+      }
+    }
+
+    if (grp == 0) {
+      if (nsplit == 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float inv = l[g] > 0.f ? 1.f / l[g] : 0.f;
+          float r0[8], r1[8];
+#pragma unroll
+          for (int d = 0; d < 8; ++d) {
+            r0[d] = o[g][d] * inv;
+            r1[d] = o[g][8 + d] * inv;
+          }
+          T* orow = out + (b * p.Hq + kvh * G + g) * kD;
+          *reinterpret_cast<uint4*>(orow + 8 * sub) = pack16<T>(r0);
+          *reinterpret_cast<uint4*>(orow + 64 + 8 * sub) = pack16<T>(r1);
+        }
+      } else {
+        const int64_t prow0 =
+            ((b * p.n_hg + hg) * (int64_t)p.max_splits + split) * heads_cta + w * G;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float* po = ws_o + (prow0 + g) * kD;
+          *reinterpret_cast<float4*>(po + 8 * sub) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+          *reinterpret_cast<float4*>(po + 8 * sub + 4) =
+              make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+          *reinterpret_cast<float4*>(po + 64 + 8 * sub) =
+              make_float4(o[g][8], o[g][9], o[g][10], o[g][11]);
+          *reinterpret_cast<float4*>(po + 64 + 8 * sub + 4) =
+              make_float4(o[g][12], o[g][13], o[g][14], o[g][15]);
+          if (sub == 0) {
+            ws_ml[(prow0 + g) * 2] = m[g];
+            ws_ml[(prow0 + g) * 2 + 1] = l[g];
+          }
+        }
+        __threadfence();
+      }
+    }
+  }
+
+  if (nsplit == 1) return;
+
+  // ---- cross-split merge by the last CTA of this (sequence, head group)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    int* ticket = tickets + b * p.n_hg + hg;
+    const int prev = atomicAdd(ticket, 1);
+    const int last = (prev == nsplit - 1);
+    if (last) atomicExch(ticket, 0);  // ready for the next launch
+    s_misc[2] = last;
+  }
+  __syncthreads();
+  if (!s_misc[2]) return;
+  __threadfence();
+  const int64_t pbase = (b * p.n_hg + hg) * (int64_t)p.max_splits * heads_cta;
+  for (int hh = threadIdx.x; hh < heads_cta; hh += blockDim.x) {
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(&ws_ml[(pbase + (int64_t)s * heads_cta + hh) * 2]));
+    float L = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const int64_t r = pbase + (int64_t)s * heads_cta + hh;
+      const float ms = __ldcg(&ws_ml[r * 2]);
+      const float wgt = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+      s_wts[hh * nsplit + s] = wgt;
+      L += wgt * __ldcg(&ws_ml[r * 2 + 1]);
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    for (int s = 0; s < nsplit; ++s) s_wts[hh * nsplit + s] *= inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < heads_cta * kD; idx += blockDim.x) {
+    const int hh = idx / kD, d = idx % kD;
+    float acc = 0.f;
+    for (int s = 0; s < nsplit; ++s)
+      acc = fmaf(s_wts[hh * nsplit + s], __ldcg(&ws_o[(pbase + (int64_t)s * heads_cta + hh) * kD + d]), acc);
+    out[(out_row0 + hh) * kD + d] = from_f32<T>(acc);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// General fallback (any D <= 256, any block size / head ratio): one CTA of
+// four warps per (sequence, query head); tokens dealt round-robin to warps,
+// one token per warp step, lanes over the head dim.  Used only for shapes the
+// TMA path does not cover.
+// ---------------------------------------------------------------------------
+template <typename T, typename IDX>
+__global__ void __launch_bounds__(128) paged_decode_generic_kernel(
+    const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
+    const IDX* __restrict__ block_table, const IDX* __restrict__ ctx_len, T* __restrict__ out,
+    int64_t Hq, int64_t Hkv, int64_t D, int64_t num_blocks, int64_t bs, int64_t max_blocks,
+    float qscale) {
+  __shared__ float s_m[4], s_l[4], s_o[4][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t hq = blockIdx.x, b = blockIdx.y;
+  const int64_t kvh = hq / (Hq / Hkv);
+  const int64_t ctx = (int64_t)ctx_len[b];
+  const int64_t nvb = ctx > 0 ? min((ctx + bs - 1) / bs, max_blocks) : 0;
+  const T* qr = q + (b * Hq + hq) * D;
+  float qv[8], ov[8];
+  for (int i = 0; i < 8; ++i) {
+    const int64_t d = lane + 32 * i;
+    qv[i] = d < D ? to_f32(qr[d]) * qscale : 0.f;
+    ov[i] = 0.f;
+  }
+  float mrun = -INFINITY, lrun = 0.f;
+  int64_t rank = 0;
+  for (int64_t j = 0; j < nvb; ++j) {
+    const IDX id = block_table[b * max_blocks + j];
+    if (bad_block(id, num_blocks)) continue;
+    int64_t nt = ctx - rank * bs;
+    ++rank;
+    nt = nt < 0 ? 0 : (nt > bs ? bs : nt);
+    for (int64_t t = warp; t < nt; t += 4) {
+      const int64_t row = (((int64_t)id * bs + t) * Hkv + kvh) * D;
+      float part = 0.f;
+      for (int i = 0; i < 8; ++i) {
+        const int64_t d = lane + 32 * i;
+        if (d < D) part = fmaf(qv[i], to_f32(kc[row + d]), part);
+      }
+      const float sc = warp_sum(part);
+      const float mn = fmaxf(mrun, sc);
+      const float a = (mrun == -INFINITY) ? 0.f : exp2f(mrun - mn);
+      const float pw = exp2f(sc - mn);
+      lrun = lrun * a + pw;
+      for (int i = 0; i < 8; ++i) {
+        const int64_t d = lane + 32 * i;
+        ov[i] = ov[i] * a + (d < D ? pw * to_f32(vc[row + d]) : 0.f);
+      }
+      mrun = mn;
+    }
+  }
+  if (lane == 0) {
+    s_m[warp] = mrun;
+    s_l[warp] = lrun;
+  }
+  for (int i = 0; i < 8; ++i) {
+    const int64_t d = lane + 32 * i;
+    if (d < D) s_o[warp][d] = ov[i];
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w]);
+  float L = 0.f, wts[4];
+  for (int w = 0; w < 4; ++w) {
+    wts[w] = (s_m[w] == -INFINITY) ? 0.f : exp2f(s_m[w] - M);
+    L += wts[w] * s_l[w];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int w = 0; w < 4; ++w) acc += wts[w] * s_o[w][d];
+    out[(b * Hq + hq) * D + d] = from_f32<T>(acc * inv);
+  }
+}
+
+struct Geometry {
+  bool tma_path;
+  int HG, n_hg, G, split_blocks, max_splits, stages;
+  uint32_t stage_bytes;
+  size_t tiles_bytes;
+  size_t smem_bytes;
+};
+
+constexpr size_t kSmemBudget = 227 * 1024;
+
+Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t bs,
+                         int64_t max_blocks, const b200_launch_cfg* cfg) {
+  Geometry g{};
+  g.tma_path = false;
+  if (Hkv <= 0 || Hq % Hkv != 0) return g;
+  g.G = (int)(Hq / Hkv);
+  int split = (cfg && cfg->split > 0) ? cfg->split : 16;
+  if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
+  g.split_blocks = split;
+  g.max_splits = (int)((max_blocks + split - 1) / split);
+  if (D != kD || !(g.G == 1 || g.G == 2 || g.G == 4 || g.G == 8) || bs > 256 || bs < 1 ||
+      g.max_splits > kMaxSplits)
+    return g;
+  // Largest head group (<= 8 warps) whose page keeps >= 3 stages in budget.
+  int HG = 0;
+  for (int cand = 8; cand >= 1; --cand) {
+    if (Hkv % cand) continue;
+    const uint64_t page = 2ull * bs * cand * kD * 2;
+    if (page * 3 + 8192 <= kSmemBudget) {
+      HG = cand;
+      break;
+    }
+  }
+  if (HG == 0) return g;
+  g.HG = HG;
+  g.n_hg = (int)(Hkv / HG);
+  g.stage_bytes = (uint32_t)(2ull * bs * HG * kD * 2);
+  int stages = (cfg && cfg->stages > 0) ? cfg->stages : 4;
+  const size_t fixed = 2 * 8 * 16 + 2 * kMaxSplitBlocks * 4 + 64;
+  while (stages > 2 && (size_t)stages * g.stage_bytes + fixed > kSmemBudget) --stages;
+  if ((size_t)stages * g.stage_bytes + fixed > kSmemBudget) return g;
+  g.stages = stages;
+  size_t tiles = (size_t)stages * g.stage_bytes;
+  const size_t wts = (size_t)HG * g.G * g.max_splits * 4;
+  if (wts > tiles) tiles = (wts + 127) / 128 * 128;
+  g.tiles_bytes = tiles;
+  g.smem_bytes = tiles + fixed;
+  if (g.smem_bytes > kSmemBudget) return g;
+  g.tma_path = true;
+  return g;
+}
+
+template <typename T, typename IDX, int G>
+int launch_tma(const void* q, const void* k_cache, const void* v_cache, const void* block_table,
+               const void* ctx_len, void* out, int64_t B, int64_t Hq, int64_t Hkv,
+               int64_t num_blocks, int64_t bs, int64_t max_blocks, float scale,
+               const Geometry& geo, void* workspace, cudaStream_t stream) {
+  CUtensorMap tk, tv;
+  const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)Hkv, (uint64_t)(num_blocks * bs)};
+  const uint64_t strides[2] = {(uint64_t)kD * 2, (uint64_t)Hkv * kD * 2};
+  const uint32_t box[3] = {(uint32_t)kD, (uint32_t)geo.HG, (uint32_t)bs};
+  const CUtensorMapDataType dt = std::is_same<T, __half>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  int st = encode_tensor_map(&tk, dt, 3, k_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st) return st;
+  st = encode_tensor_map(&tv, dt, 3, v_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st) return st;
+  DecodeParams p;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.num_blocks = num_blocks;
+  p.block_size = bs;
+  p.max_blocks = max_blocks;
+  p.HG = geo.HG;
+  p.n_hg = geo.n_hg;
+  p.split_blocks = geo.split_blocks;
+  p.max_splits = geo.max_splits;
+  p.stages = geo.stages;
+  p.stage_bytes = geo.stage_bytes;
+  p.tiles_bytes = (uint32_t)geo.tiles_bytes;
+  p.qscale = scale * 1.4426950408889634f;
+  // Workspace: [tickets (fixed region) | partials o | partials (m,l)].  The
+  // ticket region sits at a fixed offset so that calls of different shapes
+  // sharing one buffer always find their tickets at zero.
+  const size_t n_rows = (size_t)B * Hq * geo.max_splits;
+  int* tickets = static_cast<int*>(workspace);
+  float* ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTicketBytes);
+  float* ws_ml = ws_o + n_rows * kD;
+  auto kern = paged_decode_kernel<T, IDX, G>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)geo.smem_bytes);
+  if (e != cudaSuccess) return launch_status(e);
+  dim3 grid(geo.max_splits, (unsigned)B, geo.n_hg);
+  kern<<<grid, (geo.HG + 1) * 32, geo.smem_bytes, stream>>>(
+      tk, tv, static_cast<const T*>(q), static_cast<const IDX*>(block_table),
+      static_cast<const IDX*>(ctx_len), static_cast<T*>(out), ws_o, ws_ml, tickets, p);
+  return launch_status(cudaGetLastError());
+}
+
+size_t workspace_bytes_for(int64_t B, int64_t Hq, int64_t D, const Geometry& geo) {
+  if (!geo.tma_path) return 0;
+  const size_t n_rows = (size_t)B * Hq * geo.max_splits;
+  return kTicketBytes + n_rows * (size_t)(D + 2) * 4;
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq, int64_t max_blocks,
+                                                      int64_t block_size, int64_t D,
+                                                      const b200_launch_cfg* cfg) {
+  // The workspace depends on Hkv only through the head-group count, which
+  // is bounded by Hq; size for the largest case.
+  if (B <= 0 || Hq <= 0 || max_blocks <= 0 || block_size <= 0 || D <= 0) return 0;
+  Geometry g{};
+  int split = (cfg && cfg->split > 0) ? cfg->split : 16;
+  if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
+  g.tma_path = true;
+  g.max_splits = (int)((max_blocks + split - 1) / split);
+  return workspace_bytes_for(B, Hq, D, g);
+}
+
+extern "C" int b200_paged_attention(const void* q, const void* k_cache, const void* v_cache,
+                                    const void* block_table, const void* context_len, void* out,
+                                    int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                                    int64_t num_blocks, int64_t block_size, int64_t max_blocks,
+                                    float scale, int32_t dtype, int32_t index_dtype,
+                                    void* workspace, size_t workspace_bytes,
+                                    const b200_launch_cfg* cfg, void* stream) {
+  if (int e = injected_error("paged_attention")) return e;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || num_blocks <= 0 || block_size <= 0 ||
+      max_blocks <= 0 || Hq % Hkv != 0)
+    return B200_ERR_BAD_ARG;
+  if (B == 0) return B200_OK;
+  if (!q || !k_cache || !v_cache || !block_table || !context_len || !out) return B200_ERR_BAD_ARG;
+  if (index_dtype != B200_I32 && index_dtype != B200_I64) return B200_ERR_UNSUPPORTED;
+  if (B > 65535 || B * Hkv > (int64_t)(kTicketBytes / 4)) return B200_ERR_UNSUPPORTED;
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Geometry geo = choose_geometry(B, Hq, Hkv, D, block_size, max_blocks, cfg);
+  const bool aligned = aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out);
+  if (geo.tma_path && aligned && num_blocks * block_size < (1ll << 31)) {
+    const size_t need = workspace_bytes_for(B, Hq, D, geo);
+    const bool single = geo.max_splits == 1;
+    if (!single && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
+      return B200_ERR_WORKSPACE;
+    return B200_DISPATCH_HALF(dtype, [&] {
+      auto run = [&](auto idx_tag) -> int {
+        using IDX = decltype(idx_tag);
+        switch (geo.G) {
+          case 1: return launch_tma<scalar_t, IDX, 1>(q, k_cache, v_cache, block_table, context_len, out, B, Hq, Hkv, num_blocks, block_size, max_blocks, scale, geo, workspace, s);
+          case 2: return launch_tma<scalar_t, IDX, 2>(q, k_cache, v_cache, block_table, context_len, out, B, Hq, Hkv, num_blocks, block_size, max_blocks, scale, geo, workspace, s);
+          case 4: return launch_tma<scalar_t, IDX, 4>(q, k_cache, v_cache, block_table, context_len, out, B, Hq, Hkv, num_blocks, block_size, max_blocks, scale, geo, workspace, s);
+          default: return launch_tma<scalar_t, IDX, 8>(q, k_cache, v_cache, block_table, context_len, out, B, Hq, Hkv, num_blocks, block_size, max_blocks, scale, geo, workspace, s);
+        }
+      };
+      return index_dtype == B200_I32 ? run(int32_t{}) : run(int64_t{});
+    });
+  }
+  if (D > 256) return B200_ERR_UNSUPPORTED;
+  return B200_DISPATCH_HALF(dtype, [&] {
+    auto run = [&](auto idx_tag) -> int {
+      using IDX = decltype(idx_tag);
+      dim3 grid((unsigned)Hq, (unsigned)B);
+      paged_decode_generic_kernel<scalar_t, IDX><<<grid, 128, 0, s>>>(
+          static_cast<const scalar_t*>(q), static_cast<const scalar_t*>(k_cache),
+          static_cast<const scalar_t*>(v_cache), static_cast<const IDX*>(block_table),
+          static_cast<const IDX*>(context_len), static_cast<scalar_t*>(out), Hq, Hkv, D,
+          num_blocks, block_size, max_blocks, scale * 1.4426950408889634f);
+      return launch_status(cudaGetLastError());
+    };
+    return index_dtype == B200_I32 ? run(int32_t{}) : run(int64_t{});
+  });
+}
