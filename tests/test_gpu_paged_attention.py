@@ -71,15 +71,36 @@ def test_baseline_config_all_rows_vs_single_split(cuda_device):
 
 @pytest.mark.parametrize("G", [1, 2, 4, 8])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_gqa_ratios(G, dtype, cuda_device):
+@pytest.mark.parametrize("flags", [0, 1])
+def test_gqa_ratios(G, dtype, flags, cuda_device):
     Hkv = 8 if G < 8 else 4
     cache = WL.paged_cache(num_blocks=256, block_size=16, Hkv=Hkv, D=128, dtype=dtype, device=cuda_device, seed=G)
     inp = WL.decode_attention_inputs(cache, B=5, Hq=Hkv * G, ctx_lo=1, ctx_hi=700, device=cuda_device, seed=G)
-    run_and_check(inp["q"], cache.k_cache, cache.v_cache, inp["block_table"], inp["context_len"], cuda_device)
+    run_and_check(inp["q"], cache.k_cache, cache.v_cache, inp["block_table"], inp["context_len"], cuda_device,
+                  cfg={"flags": flags})
+
+
+def test_garbage_in_unused_slots_is_ignored(cuda_device):
+    """Slots past the context length inside the last page may hold anything,
+    including NaN; masked tokens must not leak into the output."""
+    cache = WL.paged_cache(num_blocks=128, block_size=16, Hkv=8, D=128, device=cuda_device, seed=11)
+    inp = WL.decode_attention_inputs(cache, B=4, Hq=32, ctx_lo=20, ctx_hi=400, device=cuda_device, seed=11)
+    bt, cl = inp["block_table"], inp["context_len"]
+    for b in range(4):
+        ctx = int(cl[b])
+        last = int(bt[b, (ctx - 1) // 16])
+        off = ctx % 16
+        if off:
+            cache.k_cache[last, off:] = float("nan")
+            cache.v_cache[last, off:] = float("nan")
+    for flags in (0, 1):
+        out = run_and_check(inp["q"], cache.k_cache, cache.v_cache, bt, cl, cuda_device, cfg={"flags": flags})
+        assert not torch.isnan(out).any()
 
 
 @pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])
-def test_edge_contexts_and_invalid_blocks(index_dtype, cuda_device):
+@pytest.mark.parametrize("flags", [0, 1])  # 1: force the CUDA-core consumer
+def test_edge_contexts_and_invalid_blocks(index_dtype, flags, cuda_device):
     cache = WL.paged_cache(num_blocks=128, block_size=16, Hkv=8, D=128, device=cuda_device, seed=3)
     B, maxb = 9, 20
     g = torch.Generator(device=cuda_device).manual_seed(5)
@@ -90,7 +111,7 @@ def test_edge_contexts_and_invalid_blocks(index_dtype, cuda_device):
     bt[8, 5] = -7
     q = torch.randn(B, 32, 128, generator=g, device=cuda_device).bfloat16()
     for split in (None, 1, 2, 3, 7):
-        cfg = {"split": split} if split else None
+        cfg = {"split": split or 0, "flags": flags}
         out = run_and_check(q, cache.k_cache, cache.v_cache, bt, cl, cuda_device, cfg=cfg)
         assert torch.count_nonzero(out[5]) == 0  # ctx 0 -> zero row
 

@@ -1,0 +1,265 @@
+"""Command line: the correctness gate and the tuner over the CUDA variants.
+
+    python -m b200ops.cli list
+    python -m b200ops.cli verify-correctness OP [--shape K=V,...] [--dtype bf16]
+    python -m b200ops.cli optimize OP [--shape ...] [--strategy grid|best_of_n|ucb|thompson|epsilon|reinforce|grpo]
+
+Pipeline glue follows the reference's triton_agent/cli.py: contracts are
+registered from ops/<op>/contract.yaml (:408-416), variants are discovered
+from ops/<op>/templates (:321-360, here cuda_v*.py), the reference function
+and input generator come from ops/<op>/reference.py (:363-390), and each
+candidate goes compile -> run -> check_numerical -> profile -> reward
+(:193-278, :705-769).  Failures are caught into compile_log/verify_log, so a
+bad launch configuration costs a candidate, not the run.
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import json
+import sys
+import time
+from pathlib import Path
+from typing import Any
+
+import click
+
+from .core.compiler import compile_kernel
+from .core.contract import OpContract
+from .core.registry import get_registry
+from .core.reward import compute_score
+from .core.spec import CandidateResult, OpAction, OpState
+from .core.verifier import check_numerical
+from .ops import OPS_DIR
+
+DTYPES = {"fp16": "float16", "bf16": "bfloat16", "fp32": "float32"}
+
+
+def ensure_registered(op: str, ops_dir: Path = OPS_DIR) -> None:
+    reg = get_registry()
+    if not reg.has(op):
+        path = ops_dir / op / "contract.yaml"
+        if path.exists():
+            reg.register(OpContract.from_yaml(path))
+
+
+def _import_path(name: str, path: Path):
+    spec = importlib.util.spec_from_file_location(name, str(path))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_templates(op: str, ops_dir: Path = OPS_DIR) -> dict[str, Any]:
+    """template_id -> factory, for every public callable of
+    ops/<op>/templates/cuda_v*.py whose name neither starts with the op name
+    nor ends with `_kernel` (the reference's discovery rule)."""
+    out: dict[str, Any] = {}
+    tdir = ops_dir / op / "templates"
+    for path in sorted(tdir.glob("cuda_v*.py")):
+        mod = _import_path(f"b200ops.ops.{op}.templates.{path.stem}", path)
+        for name in dir(mod):
+            if name.startswith("_") or name.startswith(op) or name.endswith("_kernel"):
+                continue
+            obj = getattr(mod, name)
+            if callable(obj) and not isinstance(obj, type):
+                out[f"{path.stem}.{name}"] = obj
+    return out
+
+
+def load_reference(op: str, ops_dir: Path = OPS_DIR):
+    path = ops_dir / op / "reference.py"
+    if not path.exists():
+        return None, None
+    mod = _import_path(f"b200ops.ops.{op}.reference", path)
+    return getattr(mod, op, None), getattr(mod, "generate_test_inputs", None)
+
+
+def build_compile_args(state: Any, action: OpAction, op: str) -> dict[str, Any]:
+    args = {"B": state.B, "T": state.T, "D": state.D, "BLOCK_SIZE": action.block_d,
+            "NUM_WARPS": action.num_warps, "NUM_STAGES": action.num_stages}
+    if "rope" in op:
+        args["H"] = getattr(state, "H", 32)
+    args.update({k: v for k, v in action.launch_cfg().items() if v})
+    return args
+
+
+def parse_shape(shape: str) -> dict[str, int]:
+    out = {}
+    for kv in filter(None, (s.strip() for s in shape.split(","))):
+        k, v = kv.split("=")
+        out[k.strip()] = int(v)
+    return out
+
+
+def _torch_dtype(name: str):
+    import torch
+
+    return getattr(torch, DTYPES.get(name, name))
+
+
+def _clone_inputs(inputs):
+    import torch
+
+    return tuple(x.clone() if isinstance(x, torch.Tensor) else x for x in inputs)
+
+
+def evaluate(op: str, contract: OpContract, factory, action: OpAction, state, inputs, ref_out,
+             baseline_us: float = 0.0, profile: bool = True) -> CandidateResult:
+    """compile -> run -> verify -> profile -> reward for one candidate."""
+    from .core.profiler import profile_kernel
+
+    comp = compile_kernel(factory, build_compile_args(state, action, op))
+    if not comp.success:
+        r = CandidateResult(compile_pass=False, compile_log=comp.error_log)
+        compute_score(r)
+        return r
+    run_inputs = _clone_inputs(inputs)  # in-place variants must not see earlier writes
+    try:
+        out = comp.kernel_fn(*run_inputs)
+    except Exception as e:
+        r = CandidateResult(compile_pass=True, verify_pass=False, compile_log=str(e))
+        compute_score(r)
+        return r
+    r = check_numerical(out, ref_out, contract)
+    if r.verify_pass and profile:
+        p = profile_kernel(comp.kernel_fn, run_inputs, warmup=contract.benchmark.warmup,
+                           repeat=contract.benchmark.repeat, baseline_latency_us=baseline_us)
+        p.verify_log = r.verify_log
+        r = p
+    compute_score(r)
+    return r
+
+
+@click.group()
+def main() -> None:
+    """sm_100a operator backend: correctness gate and tuner."""
+
+
+@main.command("list")
+def list_ops() -> None:
+    """Operators with a contract and a CUDA variant."""
+    for d in sorted(OPS_DIR.iterdir()):
+        if (d / "contract.yaml").exists():
+            click.echo(f"{d.name}: {', '.join(load_templates(d.name)) or '(no variants)'}")
+
+
+@main.command("verify-correctness")
+@click.argument("op")
+@click.option("--shape", default="", help="generate_test_inputs keyword arguments, e.g. B=8,T=2048,D=4096")
+@click.option("--dtype", default="fp16")
+@click.option("--json-out", default=None, help="write the per-variant results as JSON")
+def verify_correctness(op: str, shape: str, dtype: str, json_out: str | None) -> None:
+    """Checks every CUDA variant of OP against its PyTorch reference."""
+    ensure_registered(op)
+    if not get_registry().has(op):
+        raise click.ClickException(f"Operator '{op}' not found.")
+    contract = get_registry().get(op)
+    ref_fn, gen_fn = load_reference(op)
+    inputs = gen_fn(**parse_shape(shape), dtype=_torch_dtype(dtype), device="cuda")
+    ref_out = ref_fn(*_clone_inputs(inputs))
+    parsed = parse_shape(shape)
+    state = OpState(op, parsed.get("B", 8), parsed.get("T", 2048), parsed.get("D", 4096), dtype, "cuda")
+    rows = []
+    ok_all = True
+    for tid, factory in sorted(load_templates(op).items()):
+        action = OpAction(template_id=tid, block_d=256, num_warps=4, num_stages=3)
+        r = evaluate(op, contract, factory, action, state, inputs, ref_out, profile=False)
+        ok_all &= r.verify_pass
+        log = json.loads(r.verify_log) if r.verify_log.startswith("{") else {}
+        rows.append({"template": tid, "compile": r.compile_pass, "verify": r.verify_pass,
+                     "max_abs_error": log.get("max_abs_error"), "mean_abs_error": log.get("mean_abs_error"),
+                     "nan_inf": bool(log.get("has_nan") or log.get("has_inf")),
+                     "error": (r.compile_log or ("" if r.verify_pass else r.verify_log))[:200]})
+    try:
+        from rich.console import Console
+        from rich.table import Table
+
+        t = Table(title=f"Correctness: {op} ({shape or 'defaults'}, {dtype})")
+        for col in ("Template", "Compile", "Max AE", "Mean AE", "NaN/Inf", "Verdict"):
+            t.add_column(col)
+        for r in rows:
+            fmt = lambda v: "—" if v is None else f"{v:.1e}"  # noqa: E731
+            t.add_row(r["template"], "OK" if r["compile"] else "FAIL", fmt(r["max_abs_error"]),
+                      fmt(r["mean_abs_error"]), "YES" if r["nan_inf"] else "no", "PASS" if r["verify"] else "FAIL")
+        Console().print(t)
+    except ImportError:
+        for r in rows:
+            click.echo(json.dumps(r))
+    if json_out:
+        Path(json_out).write_text(json.dumps(rows, indent=2))
+    if not ok_all:
+        sys.exit(1)
+
+
+@main.command()
+@click.argument("op")
+@click.option("--shape", default="")
+@click.option("--dtype", default="fp16")
+@click.option("--strategy", default="grid",
+              type=click.Choice(["grid", "best_of_n", "ucb", "thompson", "epsilon", "reinforce", "grpo"]))
+@click.option("--max-candidates", default=16, type=int)
+@click.option("--retry", default=1, type=int)
+@click.option("--out", default="episodes", help="directory for the episode record")
+def optimize(op: str, shape: str, dtype: str, strategy: str, max_candidates: int, retry: int, out: str) -> None:
+    """Searches the CUDA launch/tile space of OP and promotes the best variant."""
+    from .agent.generator import generate_best_of_n, generate_grid
+    from .agent.promoter import should_promote
+    from .agent.repairer import repair_action, should_retry
+    from .agent.selector import select_best
+    from .core.profiler import time_device
+    from .microrl.trainer import Trainer
+
+    ensure_registered(op)
+    contract = get_registry().get(op)
+    parsed = parse_shape(shape)
+    state = OpState(op, parsed.get("B", 8), parsed.get("T", 2048), parsed.get("D", 4096), dtype, "cuda")
+    templates = load_templates(op)
+    ref_fn, gen_fn = load_reference(op)
+    inputs = gen_fn(**parsed, dtype=_torch_dtype(dtype), device="cuda")
+    ref_out = ref_fn(*_clone_inputs(inputs))
+    base_inputs = _clone_inputs(inputs)
+    lat = sorted(time_device(lambda: ref_fn(*base_inputs), warmup=3, repeat=10))
+    baseline_us = lat[len(lat) // 2]
+    state.baseline_latency_us = baseline_us
+
+    if strategy in ("grid", "best_of_n"):
+        cands = generate_grid(contract, state, templates) if strategy == "grid" else \
+            generate_best_of_n(contract, state, templates, n=max_candidates, seed=0)
+        cands = cands[:max_candidates]
+        results = [evaluate(op, contract, templates[t], a, state, inputs, ref_out, baseline_us) for t, a in cands]
+    else:
+        all_c = generate_grid(contract, state, templates)
+        trainer = Trainer(strategy=strategy, store_path=Path(out) / "best_configs.json")
+        cands, results = [], []
+        for _ in range(max_candidates):
+            i = trainer.select(all_c, state)
+            tid, action = all_c[i]
+            r = evaluate(op, contract, templates[tid], action, state, inputs, ref_out, baseline_us)
+            for _ in range(retry):
+                if r.compile_pass and r.verify_pass:
+                    break
+                fixed = repair_action(action, r)
+                if not should_retry(fixed, action, r):
+                    break
+                action = fixed
+                r = evaluate(op, contract, templates[tid], action, state, inputs, ref_out, baseline_us)
+            trainer.update(action, state, r, all_c)
+            cands.append((tid, action))
+            results.append(r)
+    best_i, best = select_best(cands, results)
+    best.promoted = should_promote(best, contract)
+    record = {"op": op, "shape": parsed, "dtype": dtype, "strategy": strategy, "baseline_latency_us": baseline_us,
+              "time": time.time(), "best": {"action": cands[best_i][1].to_dict(), "result": best.to_dict()},
+              "candidates": [{"action": a.to_dict(), "result": r.to_dict()} for (_, a), r in zip(cands, results)]}
+    outdir = Path(out) / op
+    outdir.mkdir(parents=True, exist_ok=True)
+    path = outdir / f"episode_{int(time.time())}.json"
+    path.write_text(json.dumps(record, indent=2))
+    click.echo(f"best {cands[best_i][0]} {cands[best_i][1].launch_cfg()} p50={best.latency_us_p50:.1f}us "
+               f"speedup={best.speedup:.2f}x reward={best.reward:.2f} promoted={best.promoted} -> {path}")
+
+
+if __name__ == "__main__":
+    main()

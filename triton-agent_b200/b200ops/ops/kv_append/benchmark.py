@@ -1,0 +1,8 @@
+"""Device-timed latency of the kv_append CUDA variant (role of
+triton_agent/ops/kv_append/benchmark.py), CUDA events on the launching stream."""
+
+from b200ops.core.profiler import profile_kernel
+
+
+def benchmark_kv_append(kernel_fn, inputs, warmup=20, repeat=100, flush_l2=False):
+    return profile_kernel(kernel_fn, inputs, warmup=warmup, repeat=repeat, flush_l2=flush_l2)

@@ -1,0 +1,19 @@
+"""Correctness check of the rope_kv_append_paged CUDA variant against reference.py
+(role of triton_agent/ops/rope_kv_append_paged/verify.py)."""
+
+from pathlib import Path
+
+from b200ops.core.contract import OpContract
+from b200ops.core.verifier import check_numerical
+
+_HERE = Path(__file__).resolve().parent
+
+
+def verify_rope_kv_append_paged(kernel_fn, inputs, reference_fn=None):
+    from importlib import import_module
+
+    contract = OpContract.from_yaml(_HERE / "contract.yaml")
+    ref = reference_fn or getattr(import_module("b200ops.ops.rope_kv_append_paged.reference"), "rope_kv_append_paged")
+    expected = ref(*inputs)
+    got = kernel_fn(*inputs)
+    return check_numerical(got, expected, contract)

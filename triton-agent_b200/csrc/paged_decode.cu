@@ -78,14 +78,220 @@ __device__ __forceinline__ bool bad_block(IDX id, int64_t nb) {
   return id < 0 || (int64_t)id >= nb;
 }
 
-template <typename T, typename IDX, int G>
+// ---------------------------------------------------------------------------
+// Tensor-core consumer (block size a multiple of 16).  Warp w owns kv head
+// h0 + w; its G query heads are rows 0..G-1 of a 16-row mma.sync tile (the
+// other rows are zero).  Per 16-token chunk of a page:
+//   S[16 x 16 tok] = Q[16 x 128] K^T   -- 8 k-steps x 2 n-tiles of m16n8k16,
+//                                         K fragments by ldmatrix (rows = tokens)
+//   online softmax on the C fragments: each thread holds 4 scores of head
+//   lane/4 (tokens 2(lane%4)+{0,1}, +8); the row max needs 2 xor-shuffles
+//   O[16 x 128] += P[16 x 16] V       -- P reused from the S fragments as the A
+//                                         operand, V fragments by ldmatrix.trans
+// Shared-memory tiles are SWIZZLE_128B with rows = (head, token), so the 8
+// rows of every ldmatrix matrix hit 8 distinct 16-byte bank groups.  The
+// running max is raised only when it grows by more than 2^8 (exact: O and
+// l share the offset).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  // A rows 8..15 are zero (a1, a3 = 0)
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Zeroes the 16-bit halves of a B fragment register whose token is >= ntok.
+__device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int ntok) {
+  const uint32_t lo = tok < ntok ? 0x0000ffffu : 0u;
+  const uint32_t hi = tok + 1 < ntok ? 0xffff0000u : 0u;
+  return v & (lo | hi);
+}
+
+template <typename T, int G>
+__device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
+                                            const int* list_ntok, int* s_misc, int npages, int nsplit,
+                                            const T* __restrict__ q, T* __restrict__ out,
+                                            float* __restrict__ ws_o, float* __restrict__ ws_ml, int64_t b,
+                                            int hg, int split, int w, int lane, const DecodeParams& p) {
+  const int HG = p.HG;
+  const int bs = (int)p.block_size;
+  const int64_t kvh = (int64_t)hg * HG + w;
+  const int qh = lane >> 2;        // query head row of this thread (valid if < G)
+  const int qc = (lane & 3) * 2;   // column pair inside an 8-wide n-tile
+  // Q fragments (A operand), rows >= G are zero.
+  uint32_t qa[8][2];
+  {
+    const T* qr = q + (b * p.Hq + kvh * G + (qh < G ? qh : 0)) * kD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + qc) : 0u;
+      qa[ks][1] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + qc) : 0u;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_used = -INFINITY, l_part = 0.f;
+  const float sl2 = p.qscale;
+  const uint32_t base = sm100::smem_u32(smem);
+  const uint32_t hbytes = p.stage_bytes / 4;
+  const int mat = lane >> 3, mrow = lane & 7;
+
+  for (int i = 0; i < npages; ++i) {
+    const int s = i % p.stages;
+    if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+      b200_dev_error(kDevErrTimeoutFull);
+      atomicExch(&s_misc[1], 1);
+      break;
+    }
+    if (*(volatile int*)&s_misc[1]) break;
+    const int ntok = list_ntok[i];
+    const uint32_t kb = base + s * p.stage_bytes;
+    const uint32_t vb = kb + 2 * hbytes;
+    for (int t0 = 0; t0 < ntok; t0 += 16) {
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      {
+        // lane supplies row `mrow` of matrix `mat`: (n-tile mat>>1, d-chunk parity mat&1)
+        const int row = w * bs + t0 + (mat >> 1) * 8 + mrow;
+        const uint32_t rbase = kb + row * 128;
+        const int sw = row & 7;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int chunk = ((ks & 3) << 1) | (mat & 1);
+          uint32_t b00, b01, b10, b11;
+          ldsm_x4(rbase + (ks >> 2) * hbytes + ((chunk ^ sw) << 4), b00, b01, b10, b11);
+          mma16816<T>(sc[0], qa[ks][0], qa[ks][1], b00, b01);
+          mma16816<T>(sc[1], qa[ks][0], qa[ks][1], b10, b11);
+        }
+      }
+      float x[4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tok = t0 + nt * 8 + qc + e;
+          x[nt * 2 + e] = tok < ntok ? sc[nt][e] * sl2 : -INFINITY;
+        }
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (m_used == -INFINITY) {
+        m_used = mx;
+      } else if (mx > m_used + 8.0f) {
+        const float alpha = exp2f(m_used - mx);
+        m_used = mx;
+        l_part *= alpha;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          o[j][0] *= alpha;
+          o[j][1] *= alpha;
+        }
+      }
+      float pv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        pv[j] = exp2f(x[j] - m_used);
+        l_part += pv[j];
+      }
+      const uint32_t pa0 = pack_pair<T>(pv[0], pv[1]);  // tokens qc+{0,1}
+      const uint32_t pa2 = pack_pair<T>(pv[2], pv[3]);  // tokens 8+qc+{0,1}
+      const bool partial = (t0 + 16 > ntok);
+      {
+        // matrix `mat`: token half mat&1, d-chunk offset mat>>1
+        const int row = w * bs + t0 + (mat & 1) * 8 + mrow;
+        const uint32_t rbase = vb + row * 128;
+        const int sw = row & 7;
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          const int d0 = np * 16 + (mat >> 1) * 8;
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_t(rbase + (d0 >> 6) * hbytes + ((((d0 & 63) >> 3) ^ sw) << 4), v0, v1, v2, v3);
+          if (partial) {
+            v0 = mask_pair(v0, t0 + qc, ntok);
+            v1 = mask_pair(v1, t0 + 8 + qc, ntok);
+            v2 = mask_pair(v2, t0 + qc, ntok);
+            v3 = mask_pair(v3, t0 + 8 + qc, ntok);
+          }
+          mma16816<T>(o[2 * np], pa0, pa2, v0, v1);
+          mma16816<T>(o[2 * np + 1], pa0, pa2, v2, v3);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&empty_bar[s]));
+  }
+
+  float l = l_part;
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (qh >= G) return;
+  const int64_t qrow = b * p.Hq + kvh * G + qh;
+  if (nsplit == 1) {
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    T* orow = out + qrow * kD;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      *reinterpret_cast<uint32_t*>(orow + 8 * j + qc) = pack_pair<T>(o[j][0] * inv, o[j][1] * inv);
+  } else {
+    const int heads_cta = HG * G;
+    const int64_t prow = ((b * p.n_hg + hg) * (int64_t)p.max_splits + split) * heads_cta + w * G + qh;
+    float* po = ws_o + prow * kD;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) *reinterpret_cast<float2*>(po + 8 * j + qc) = make_float2(o[j][0], o[j][1]);
+    if ((lane & 3) == 0) {
+      ws_ml[prow * 2] = m_used;
+      ws_ml[prow * 2 + 1] = l;
+    }
+    __threadfence();
+  }
+}
+
+template <typename T, typename IDX, int G, bool MMA>
 __global__ void __launch_bounds__(288, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const T* __restrict__ q,
                         const IDX* __restrict__ block_table, const IDX* __restrict__ ctx_len,
                         T* __restrict__ out, float* __restrict__ ws_o, float* __restrict__ ws_ml,
                         int* __restrict__ tickets, DecodeParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // SWIZZLE_128B tiles need 1024-byte alignment (the launch reserves the slack).
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x;
   const int64_t b = blockIdx.y;
@@ -125,15 +331,26 @@ __global__ void __launch_bounds__(288, 1)
 
   // ---- page list: valid blocks of this split with their surviving tokens
   if (warp == HG) {
+    // Invalid entries before this split shift the token ranks of its pages.
+    // Eight independent loads per lane are in flight per round.
     int inval = 0;
-    for (int j = lane; j < p0; j += 32) inval += bad_block(bt[j], p.num_blocks) ? 1 : 0;
+    for (int j0 = 0; j0 < p0; j0 += 256) {
+      IDX v[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int j = j0 + r * 32 + lane;
+        v[r] = j < p0 ? __ldg(&bt[j]) : (IDX)0;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) inval += (j0 + r * 32 + lane < p0 && bad_block(v[r], p.num_blocks)) ? 1 : 0;
+    }
     inval = __reduce_add_sync(0xffffffffu, inval);
     int count = 0;
     const unsigned lt_mask = (1u << lane) - 1u;
     for (int j0 = p0; j0 < p1; j0 += 32) {
       const int j = j0 + lane;
       const bool in = j < p1;
-      const IDX id = in ? bt[j] : (IDX)-1;
+      const IDX id = in ? __ldg(&bt[j]) : (IDX)-1;
       const bool valid = in && !bad_block(id, p.num_blocks);
       const unsigned ib = __ballot_sync(0xffffffffu, in && !valid);
       const int64_t rank = (int64_t)j - (inval + __popc(ib & lt_mask));
@@ -186,8 +403,18 @@ __global__ void __launch_bounds__(288, 1)
         sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
         const int32_t tok0 = list_id[i] * (int32_t)bs;
         const uint32_t dst = base + s * p.stage_bytes;
-        sm100::tma_load_3d(dst, &tm_k, fb, 0, hg * HG, tok0);
-        sm100::tma_load_3d(dst + p.stage_bytes / 2, &tm_v, fb, 0, hg * HG, tok0);
+        if constexpr (MMA) {
+          // [d-half][head][token][64 dims], SWIZZLE_128B (map dims: d, slot, head)
+          const uint32_t hb = p.stage_bytes / 4;
+          sm100::tma_load_3d(dst, &tm_k, fb, 0, tok0, hg * HG);
+          sm100::tma_load_3d(dst + hb, &tm_k, fb, 64, tok0, hg * HG);
+          sm100::tma_load_3d(dst + 2 * hb, &tm_v, fb, 0, tok0, hg * HG);
+          sm100::tma_load_3d(dst + 3 * hb, &tm_v, fb, 64, tok0, hg * HG);
+        } else {
+          // [token][head][128 dims], no swizzle (map dims: d, head, slot)
+          sm100::tma_load_3d(dst, &tm_k, fb, 0, hg * HG, tok0);
+          sm100::tma_load_3d(dst + p.stage_bytes / 2, &tm_v, fb, 0, hg * HG, tok0);
+        }
         ++issued;
       }
       // Never leave the CTA with bulk copies still landing in shared memory:
@@ -198,6 +425,9 @@ __global__ void __launch_bounds__(288, 1)
           b200_dev_error(kDevErrTimeoutFull);
       }
     }
+  } else if constexpr (MMA) {
+    consume_mma<T, G>(smem, full_bar, empty_bar, list_ntok, s_misc, npages, nsplit, q, out, ws_o, ws_ml,
+                      b, hg, split, warp, lane, p);
   } else {
     // ---------------------------------------------------------- consumers
     const int w = warp;
@@ -476,6 +706,7 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(
 
 struct Geometry {
   bool tma_path;
+  bool mma;  // tensor-core consumer (block size a multiple of 16)
   int HG, n_hg, G, split_blocks, max_splits, stages;
   uint32_t stage_bytes;
   size_t tiles_bytes;
@@ -490,16 +721,18 @@ Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t 
   g.tma_path = false;
   if (Hkv <= 0 || Hq % Hkv != 0) return g;
   g.G = (int)(Hq / Hkv);
-  int split = (cfg && cfg->split > 0) ? cfg->split : 16;
+  int split = (cfg && cfg->split > 0) ? cfg->split : 64;
   if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
   g.split_blocks = split;
   g.max_splits = (int)((max_blocks + split - 1) / split);
   if (D != kD || !(g.G == 1 || g.G == 2 || g.G == 4 || g.G == 8) || bs > 256 || bs < 1 ||
       g.max_splits > kMaxSplits)
     return g;
-  // Largest head group (<= 8 warps) whose page keeps >= 3 stages in budget.
+  // Largest head group (<= 8 warps, or cfg->rows_per_cta) whose page keeps
+  // >= 3 stages in budget.
   int HG = 0;
-  for (int cand = 8; cand >= 1; --cand) {
+  const int hg_max = (cfg && cfg->rows_per_cta > 0 && cfg->rows_per_cta <= 8) ? cfg->rows_per_cta : 8;
+  for (int cand = hg_max; cand >= 1; --cand) {
     if (Hkv % cand) continue;
     const uint64_t page = 2ull * bs * cand * kD * 2;
     if (page * 3 + 8192 <= kSmemBudget) {
@@ -510,9 +743,10 @@ Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t 
   if (HG == 0) return g;
   g.HG = HG;
   g.n_hg = (int)(Hkv / HG);
+  g.mma = (bs % 16 == 0) && !(cfg && (cfg->flags & 1));  // flags bit 0: force the CUDA-core consumer
   g.stage_bytes = (uint32_t)(2ull * bs * HG * kD * 2);
   int stages = (cfg && cfg->stages > 0) ? cfg->stages : 4;
-  const size_t fixed = 2 * 8 * 16 + 2 * kMaxSplitBlocks * 4 + 64;
+  const size_t fixed = 2 * 8 * 16 + 2 * kMaxSplitBlocks * 4 + 64 + 1024;  // + alignment slack
   while (stages > 2 && (size_t)stages * g.stage_bytes + fixed > kSmemBudget) --stages;
   if ((size_t)stages * g.stage_bytes + fixed > kSmemBudget) return g;
   g.stages = stages;
@@ -532,16 +766,28 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
                int64_t num_blocks, int64_t bs, int64_t max_blocks, float scale,
                const Geometry& geo, void* workspace, cudaStream_t stream) {
   CUtensorMap tk, tv;
-  const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)Hkv, (uint64_t)(num_blocks * bs)};
-  const uint64_t strides[2] = {(uint64_t)kD * 2, (uint64_t)Hkv * kD * 2};
-  const uint32_t box[3] = {(uint32_t)kD, (uint32_t)geo.HG, (uint32_t)bs};
   const CUtensorMapDataType dt = std::is_same<T, __half>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  int st = encode_tensor_map(&tk, dt, 3, k_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (st) return st;
-  st = encode_tensor_map(&tv, dt, 3, v_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (st) return st;
+  if (geo.mma) {
+    // dims (d, token slot, head): boxes of 64 dims x bs tokens x HG heads land
+    // as rows ordered (head, token) of 128 bytes, swizzled in 8-row atoms.
+    const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)(num_blocks * bs), (uint64_t)Hkv};
+    const uint64_t strides[2] = {(uint64_t)Hkv * kD * 2, (uint64_t)kD * 2};
+    const uint32_t box[3] = {64u, (uint32_t)bs, (uint32_t)geo.HG};
+    int st = encode_tensor_map(&tk, dt, 3, k_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_tensor_map(&tv, dt, 3, v_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  } else {
+    const uint64_t dims[3] = {(uint64_t)kD, (uint64_t)Hkv, (uint64_t)(num_blocks * bs)};
+    const uint64_t strides[2] = {(uint64_t)kD * 2, (uint64_t)Hkv * kD * 2};
+    const uint32_t box[3] = {(uint32_t)kD, (uint32_t)geo.HG, (uint32_t)bs};
+    int st = encode_tensor_map(&tk, dt, 3, k_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    st = encode_tensor_map(&tv, dt, 3, v_cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+  }
   DecodeParams p;
   p.B = B;
   p.Hq = Hq;
@@ -564,7 +810,7 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
   int* tickets = static_cast<int*>(workspace);
   float* ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTicketBytes);
   float* ws_ml = ws_o + n_rows * kD;
-  auto kern = paged_decode_kernel<T, IDX, G>;
+  auto kern = geo.mma ? paged_decode_kernel<T, IDX, G, true> : paged_decode_kernel<T, IDX, G, false>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)geo.smem_bytes);
   if (e != cudaSuccess) return launch_status(e);
@@ -593,7 +839,7 @@ extern "C" size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq, int
   // is bounded by Hq; size for the largest case.
   if (B <= 0 || Hq <= 0 || max_blocks <= 0 || block_size <= 0 || D <= 0) return 0;
   Geometry g{};
-  int split = (cfg && cfg->split > 0) ? cfg->split : 16;
+  int split = (cfg && cfg->split > 0) ? cfg->split : 64;
   if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
   g.tma_path = true;
   g.max_splits = (int)((max_blocks + split - 1) / split);

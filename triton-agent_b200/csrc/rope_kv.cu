@@ -187,6 +187,99 @@ __global__ void __launch_bounds__(1024) rope_kv_append_paged_kernel(
   }
 }
 
+// Single-pass variant of the fused decode step for the vectorised case
+// (every row group of tpr threads covers one row in one pass).  All loads
+// that do not depend on each other are issued first -- the token's slot and
+// position, the thread's two source chunks, the collision scan -- so the
+// critical path is two memory round trips (source / position, then the
+// cos/sin row) instead of one per dependent step.
+template <typename CS, int VN>
+__device__ __forceinline__ void load_cs(const CS* p, float* out) {
+  if constexpr (sizeof(CS) == 4) {
+#pragma unroll
+    for (int c = 0; c < VN / 4; ++c) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p) + c);
+      out[4 * c] = v.x;
+      out[4 * c + 1] = v.y;
+      out[4 * c + 2] = v.z;
+      out[4 * c + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < VN / 8; ++c) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p) + c);
+      unpack16<CS>(raw, out + 8 * c);
+    }
+  }
+}
+
+template <typename T, typename CS>
+__global__ void __launch_bounds__(1024) rope_kv_append_paged_fast_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const int64_t* __restrict__ positions, const CS* __restrict__ cos,
+    const CS* __restrict__ sin, int64_t cs_rows, const int64_t* __restrict__ slots,
+    T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t n_tok,
+    int Hq, int Hkv, int64_t D, int64_t slot_hi, int tpr) {
+  constexpr int VN = Vec<T>::N;
+  const int64_t t = blockIdx.x;
+  const int64_t half = D / 2;
+  const int nq = q ? Hq : 0;
+  const int total_rows = nq + 2 * Hkv;
+  const int row = threadIdx.x / tpr;
+  const int c = threadIdx.x % tpr;
+  const bool active = row < total_rows && c < half / VN;
+  // ---- independent loads
+  int64_t pos = positions ? __ldg(&positions[t]) : t;
+  const int64_t slot = __ldg(&slots[t]);
+  const T* src = nullptr;
+  if (row < nq) src = q + (t * Hq + row) * D;
+  else if (row < nq + Hkv) src = k + (t * Hkv + (row - nq)) * D;
+  else src = v + (t * Hkv + (row - nq - Hkv)) * D;
+  uint4 a = make_uint4(0, 0, 0, 0), b = a;
+  if (active) {
+    a = __ldg(reinterpret_cast<const uint4*>(src + c * VN));
+    b = __ldg(reinterpret_cast<const uint4*>(src + half + c * VN));
+  }
+  // collision scan: does a later token write the same slot?
+  int hit = 0;
+  for (int64_t j = t + 1 + threadIdx.x; j < n_tok; j += blockDim.x) hit |= (__ldg(&slots[j]) == slot);
+  const bool pos_ok = pos >= 0 && pos < cs_rows;
+  if (!pos_ok) pos = 0;
+  float cv[VN], sv[VN];
+  const bool rope_row = row < nq + Hkv;
+  if (active && rope_row) {
+    load_cs<CS, VN>(cos + pos * D + c * VN, cv);
+    load_cs<CS, VN>(sin + pos * D + c * VN, sv);
+  }
+  const bool later = __syncthreads_or(hit) != 0;
+  const bool write_kv = pos_ok && slot >= 0 && slot < slot_hi && !later;
+  if (!active) return;
+  T* dst;
+  if (row < nq) {
+    if (!pos_ok) return;
+    dst = q_out + (t * Hq + row) * D;
+  } else {
+    if (!write_kv) return;
+    dst = (row < nq + Hkv) ? k_cache + (slot * Hkv + (row - nq)) * D
+                           : v_cache + (slot * Hkv + (row - nq - Hkv)) * D;
+  }
+  if (rope_row) {
+    float x1[VN], x2[VN], y1[VN], y2[VN];
+    unpack16<T>(a, x1);
+    unpack16<T>(b, x2);
+#pragma unroll
+    for (int j = 0; j < VN; ++j) {
+      y1[j] = __fsub_rn(__fmul_rn(x1[j], cv[j]), __fmul_rn(x2[j], sv[j]));
+      y2[j] = __fadd_rn(__fmul_rn(x2[j], cv[j]), __fmul_rn(x1[j], sv[j]));
+    }
+    *reinterpret_cast<uint4*>(dst + c * VN) = pack16<T>(y1);
+    *reinterpret_cast<uint4*>(dst + half + c * VN) = pack16<T>(y2);
+  } else {
+    *reinterpret_cast<uint4*>(dst + c * VN) = a;
+    *reinterpret_cast<uint4*>(dst + half + c * VN) = b;
+  }
+}
+
 int threads_for(int64_t rows, int tpr, const b200_launch_cfg* cfg) {
   int64_t want = rows * tpr;
   int threads = (cfg && cfg->threads > 0) ? cfg->threads : (int)((want + 31) / 32 * 32);
@@ -377,6 +470,14 @@ int launch_fused(const void* q, const void* k, const void* v, const int64_t* pos
   auto* vc = static_cast<T*>(v_cache);
   auto* cp = static_cast<const CS*>(cos);
   auto* sp = static_cast<const CS*>(sin);
+  const bool cs_vec = aligned16(cos) && aligned16(sin) && (D * (int64_t)sizeof(CS)) % 16 == 0 &&
+                      (VN * (int64_t)sizeof(CS)) % 16 == 0;
+  if (vec && cs_vec && rows * tpr <= 1024 && !(cfg && cfg->threads > 0)) {
+    const int th = (int)(((rows * tpr) + 31) / 32 * 32);
+    rope_kv_append_paged_fast_kernel<T, CS><<<(unsigned)n_tok, th, 0, s>>>(
+        qp, kp, vp, positions, cp, sp, cs_rows, slots, qo, kc, vc, n_tok, (int)Hq, (int)Hkv, D, slot_hi, tpr);
+    return launch_status(cudaGetLastError());
+  }
   if (vec)
     rope_kv_append_paged_kernel<T, CS, true><<<(unsigned)n_tok, threads, 0, s>>>(
         qp, kp, vp, positions, cp, sp, cs_rows, slots, qo, kc, vc, n_tok, (int)Hq, (int)Hkv, D,

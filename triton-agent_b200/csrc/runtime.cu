@@ -135,6 +135,7 @@ const char* b200_kernel_list(void) {
          "rope_kernel\n"
          "kv_scatter_kernel\n"
          "rope_kv_append_paged_kernel\n"
+         "rope_kv_append_paged_fast_kernel\n"
          "paged_decode_kernel\n"
          "int8_gemm_tcgen05_kernel\n"
          "int8_splitk_reduce_kernel\n"
