@@ -20,9 +20,9 @@ def allgather_columns(local: torch.Tensor, N: int, group=None) -> torch.Tensor:
 
     world = dist.get_world_size(group)
     M, n_blk = local.shape
-    buf = torch.empty(world, M, n_blk, dtype=local.dtype, device=local.device)
+    buf = torch.empty(world * M, n_blk, dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
-    return buf.permute(1, 0, 2).reshape(M, world * n_blk)[:, :N]
+    return buf.view(world, M, n_blk).permute(1, 0, 2).reshape(M, world * n_blk)[:, :N]
 
 
 def sharded_int8_gemm(A, W_local, sA, sW_local, N: int, gemm, out_dtype=torch.float16, group=None):
