@@ -175,6 +175,26 @@ int b200_paged_attention(const void* q, const void* k_cache,
                          size_t workspace_bytes, const b200_launch_cfg* cfg,
                          void* stream);
 
+/* ---- allocation-free paged attention ---------------------------------------
+ * No counterpart in the reference.  Same arguments, semantics and results as
+ * b200_paged_attention, without the workspace: for callers that cannot
+ * allocate device memory (a C-FFI host runtime that holds only the pointers
+ * it is given, or a request path where cudaMalloc is forbidden because it can
+ * synchronise the device), the split-KV scratch is a static 16 MiB device
+ * array inside the library (per GPU, kept until exit).  Calls needing more
+ * scratch than that return B200_ERR_WORKSPACE with the size in
+ * b200_last_error_detail().  The first call on a device looks up the array's
+ * address (do it before any stream capture).  All calls share the array:
+ * calls whose executions overlap on the GPU race and must be serialised. */
+int b200_paged_attention_noalloc(const void* q, const void* k_cache,
+                                 const void* v_cache, const void* block_table,
+                                 const void* context_len, void* out, int64_t B,
+                                 int64_t Hq, int64_t Hkv, int64_t D,
+                                 int64_t num_blocks, int64_t block_size,
+                                 int64_t max_blocks, float scale, int32_t dtype,
+                                 int32_t index_dtype,
+                                 const b200_launch_cfg* cfg, void* stream);
+
 /* ---- INT8 GEMM with fused dequant epilogue --------------------------------
  * Restates triton_agent/ops/quant_matmul/reference.py:26-27 for
  * pre-quantised operands:

@@ -94,6 +94,10 @@ SIGNATURES = {
         [P, P, P, P, P, P, I64_, I64_, I64_, I64_, I64_, I64_, I64_, c_float, c_int32, c_int32, P, c_size_t,
          PCFG, P],
     ),
+    "b200_paged_attention_noalloc": (
+        c_int,
+        [P, P, P, P, P, P, I64_, I64_, I64_, I64_, I64_, I64_, I64_, c_float, c_int32, c_int32, PCFG, P],
+    ),
     "b200_int8_gemm_workspace_size": (c_size_t, [I64_, I64_, I64_, PCFG]),
     "b200_int8_gemm": (c_int, [P, P, P, P, P, I64_, I64_, I64_, I64_, c_int32, P, P, c_size_t, PCFG, P]),
     "b200_quantize_int8": (c_int, [P, P, P, I64_, I64_, c_int32, c_int32, PCFG, P]),

@@ -25,6 +25,9 @@
 //   workspace and the last CTA to finish (atomic ticket) merges them and
 //   resets the ticket, so one launch does the whole op.
 #include <math.h>
+#include <stdio.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -897,4 +900,83 @@ extern "C" int b200_paged_attention(const void* q, const void* k_cache, const vo
     };
     return index_dtype == B200_I32 ? run(int32_t{}) : run(int64_t{});
   });
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free paged attention.
+//
+// Some callers of this library cannot allocate device memory: a host runtime
+// that binds the library through a plain C FFI and only holds the device
+// pointers handed to it (it has no device allocator of its own), or a serving
+// loop that forbids cudaMalloc/cudaFree on its request path because those calls
+// can synchronise the device and would fragment memory that another allocator
+// owns.  b200_paged_attention needs a split-KV workspace from its caller;
+// this entry point instead uses a fixed scratch array compiled into the
+// library, so the caller passes only inputs and outputs.
+//
+// The scratch is kNoAllocScratchBytes of device memory per GPU that loads the
+// library, held until the process exits.  Its device address is looked up once
+// per device (cudaGetSymbolAddress with that device current) by the first call
+// made on that device, so that first call should come before any stream
+// capture.  Every call shares the one array and leaves its contents behind;
+// the ticket counters that must start at zero are cleared at the start of each
+// call.  Calls whose executions overlap on the GPU (different streams, or
+// several host threads) race on the scratch and must be serialised by the
+// caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device (set up once).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return b200::launch_status(e);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return B200_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return b200::launch_status(e);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" int b200_paged_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                            const void* block_table, const void* context_len, void* out,
+                                            int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t num_blocks,
+                                            int64_t block_size, int64_t max_blocks, float scale,
+                                            int32_t dtype, int32_t index_dtype, const b200_launch_cfg* cfg,
+                                            void* stream) {
+  if (int e = b200::injected_error("paged_attention_noalloc")) return e;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || num_blocks <= 0 || block_size <= 0 || max_blocks <= 0)
+    return B200_ERR_BAD_ARG;
+  const size_t need = b200_paged_attention_workspace_size(B, Hq, max_blocks, block_size, D, cfg);
+  if (need > kNoAllocScratchBytes) {
+    char msg[160];
+    snprintf(msg, sizeof(msg),
+             "paged_attention_noalloc: needs %zu bytes of scratch, the static scratch holds %zu", need,
+             kNoAllocScratchBytes);
+    b200::set_last_error_detail(msg);
+    return B200_ERR_WORKSPACE;
+  }
+  if (B == 0) return B200_OK;
+  void* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  // Ticket counters (one int per sequence x kv head at most) start at zero.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)B * Hkv * sizeof(int), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return b200::launch_status(e);
+  return b200_paged_attention(q, k_cache, v_cache, block_table, context_len, out, B, Hq, Hkv, D, num_blocks,
+                              block_size, max_blocks, scale, dtype, index_dtype, scratch, kNoAllocScratchBytes,
+                              cfg, stream);
 }
