@@ -135,8 +135,58 @@ def measured_peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d.get("hbm_gbs"), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def _median_us(fn, warmup=3, repeat=20, flush_l2=False):
+    from b200ops.core.profiler import time_device
+
+    lat = sorted(time_device(fn, warmup, repeat, flush_l2=flush_l2))
+    return lat[len(lat) // 2]
+
+
+def secondary_ops(dev) -> dict:
+    """The other operators of the hot path, each timed alone with CUDA events
+    on the current stream (medians of 20): INT8 GEMM (the metric's second
+    part), causal flash prefill, rmsnorm.  INT8 peak: no measured INT8 figure
+    exists for this pool, so the fraction is against 2x the measured dense
+    bf16 GEMM (the tensor core's int8:bf16 rate is 2:1) and cuBLAS int8 is
+    timed beside it on the same shapes."""
+    from b200ops import workloads as WL
+    from b200ops.runtime import ops as K
+
+    peaks = measured_peaks()
+    int8_peak = 2 * peaks["bf16_tflops"]
+    res = {}
+    for M, N in ((4096, 14336), (4096, 4096), (16, 14336)):
+        A, W, sA, sW = WL.int8_gemm_inputs(M, N, 4096, device=dev)
+        C = torch.empty(M, N, dtype=torch.float16, device=dev)
+        us = _median_us(lambda: K.int8_gemm(A, W, sA, sW, out=C), flush_l2=True)
+        ops = 2 * M * N * 4096
+        entry = {"us": us, "TOPS": ops / us / 1e6, "peak_TOPS": int8_peak, "frac": ops / us / 1e6 / int8_peak,
+                 "peak_src": f"2x {peaks['src']} bf16"}
+        if M == 16:
+            nbytes = N * 4096 + M * 4096 + 4 * (M + N) + 2 * M * N
+            entry.update({"bound": "hbm", "GBps": nbytes / us / 1e3, "hbm_frac": nbytes / us / 1e3 / peaks["hbm_gbs"]})
+        else:
+            try:
+                cu = _median_us(lambda: torch._int_mm(A, W.t()), flush_l2=True)
+                entry["cublas_int_mm_TOPS"] = ops / cu / 1e6
+            except Exception as e:  # cuBLAS int8 needs M > 16
+                entry["cublas_int_mm_TOPS"] = None
+        res[f"int8_gemm_M{M}_N{N}_K4096"] = entry
+    q, k, v = WL.flash_inputs(device=dev)
+    us = _median_us(lambda: K.flash_attn(q, k, v, causal=True), 2, 10)
+    fl = WL.causal_flops(4, 32, 4096, 128)
+    res["flash_prefill_causal_B4_H32_T4096_D128"] = {"us": us, "TFLOPs": fl / us / 1e6,
+                                                     "frac": fl / us / 1e6 / peaks["bf16_tflops"]}
+    x, w = WL.rmsnorm_inputs(device=dev)
+    y = torch.empty_like(x)
+    us = _median_us(lambda: K.rmsnorm(x, w, out=y), flush_l2=True)
+    nb = 2 * x.numel() * 4 + 4096 * 4
+    res["rmsnorm_fp32_8x2048x4096"] = {"us": us, "GBps": nb / us / 1e3, "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    return res
 
 
 # --------------------------------------------------------------------------- B200
@@ -314,6 +364,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the per-op lines (GEMM, prefill, rmsnorm)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.impl == "reference":
@@ -324,6 +375,10 @@ def main():
     dist = init_dist(ws)
     try:
         res = run_b200(args, ws, rank, local, dist)
+        if not args.no_secondary:
+            sec = secondary_ops(torch.device("cuda", local))
+            if rank == 0:
+                res["secondary"] = sec
         if rank == 0:
             if ws == 1 and not args.no_cpu_baseline:
                 torch.set_num_threads(os.cpu_count() or 1)

@@ -72,6 +72,13 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
   asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+// 2^x with the MUFU approximation (PTX ex2.approx.ftz.f32); 2^-inf = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
@@ -254,35 +261,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tmem_wait_ld();
       const int64_t k0 = (int64_t)j * kBN;
       const bool need_mask = (k0 + kBN > p.S) || (p.causal && k0 + kBN - 1 > qrow);
-      float mx = -INFINITY;
+      if (need_mask) {
+        // keys past the end or (causal) after this query row drop out
+        const int64_t lim = (p.causal && qrow + 1 < p.S) ? qrow + 1 : p.S;
+        const int64_t nv = lim - k0;
+        const int valid = nv <= 0 ? 0 : (nv >= kBN ? kBN : (int)nv);
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        float x = __uint_as_float(sr[c]) * p.sl2;
-        if (need_mask) {
-          const int64_t key = k0 + c;
-          if (key >= p.S || (p.causal && key > qrow)) x = -INFINITY;
-        }
-        sr[c] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < kBN; ++c)
+          if (c >= valid) sr[c] = __float_as_uint(-INFINITY);
       }
+      // row max of the raw scores: 8 independent chains
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sr[i]);
+#pragma unroll
+      for (int c = 8; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.sl2;
       float alpha = 1.f;
       bool rescale = false;
       if (m_used == -INFINITY) {
         m_used = mx;
       } else if (mx > m_used + kRescaleThreshold) {
-        alpha = exp2f(m_used - mx);
+        alpha = ex2_approx(m_used - mx);
         m_used = mx;
         rescale = true;
       }
-      float sum = 0.f;
+      // p = 2^(s * scale * log2 e - m): one FMA and one ex2 per score
+      const float neg_m = -m_used;
+      float sum8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
-        const float p0 = exp2f(__uint_as_float(sr[c]) - m_used);
-        const float p1 = exp2f(__uint_as_float(sr[c + 1]) - m_used);
-        sum += p0 + p1;
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c]), p.sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), p.sl2, neg_m));
+        sum8[(c >> 1) & 7] += p0 + p1;
         pk[c / 2] = pack2<T>(p0, p1);
       }
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l = l * alpha + sum;
       // PV_{j-1} must be complete before P is overwritten or O is rescaled.
       if (j > 0 && !sm100::mbar_wait(sm100::smem_u32(o_done), (j - 1) & 1)) {

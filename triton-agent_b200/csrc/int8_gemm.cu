@@ -6,21 +6,27 @@
 // for pre-quantised operands: A [M,K] int8, W [N,K] int8 (K-major, i.e. the
 // reference's b_q transposed), per-row sA [M] and per-column sW [N] fp32.
 // acc = sum_k A[m,k]*W[n,k] is exact in int32 (|acc| <= K*127^2 < 2^31 for
-// K < 133k); C = out(((float)acc * sA[m]) * sW[n]) with both products
+// K <= 131072); C = out(((float)acc * sA[m]) * sW[n]) with both products
 // rounded separately, as the reference's eager fp32 multiplies are.
 //
-// CTA tile 128 x BN (BN = 128 or 256), K step 128 bytes per stage:
-//   warp 0      TMA producer: A box {128 K, 128 M} and W box {128 K, BN N},
-//               SWIZZLE_128B, into a ring of `stages` shared-memory slots
-//   warp 1      allocates BN TMEM columns; one lane issues 4 x
-//               tcgen05.mma (M=128, N=BN, K=32) per stage and commits each
-//               stage back to the producer's "empty" barrier
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, dequant,
-//               store (warp w reads TMEM lanes 32*(w%4) .. +31)
-// Split-K (small M): each split writes its int32 partial tile to the
-// workspace; the last split to finish (atomic ticket) sums the partials in
-// a fixed order and runs the epilogue, so results stay exact and
-// deterministic.  No cluster multicast: every CTA loads its own tiles.
+// Two kernels, both fed by TMA (SWIZZLE_128B, K-major, no cluster multicast):
+//
+// int8_gemm_tcgen05_kernel -- persistent, one CTA per SM, 128 x BN output
+//   tiles (BN = 128 or 256) taken round-robin in m-fastest order (CTAs
+//   running together share W panels in L2).  Warp 0: TMA producer streaming
+//   A {128 K x 128 M} and W {128 K x BN N} boxes into a ring of stages,
+//   continuously across tiles.  Warp 1: allocates 2 x BN TMEM columns (two
+//   accumulators) and one lane issues 4 tcgen05.mma (M=128, N=BN, K=32) per
+//   stage.  Warps 2..5: epilogue, tcgen05.ld 32x32b.x32, dequant, 16-byte
+//   stores.  The accumulator of tile i drains while tile i+1 accumulates in
+//   the other half of TMEM, so the epilogue is off the tensor pipe's path.
+//
+// int8_gemm_skinny_kernel -- small M (<= 64, decode-time activations).  The
+//   operands are swapped so W rows fill the 128-row side of the MMA and the
+//   M activation rows its N side (16..64); the accumulator tile is
+//   C^T[128 n x M].  K is split across CTAs so enough SMs stream W; split
+//   partials are summed exactly with int32 red.add into a workspace tile and
+//   the last split (atomic ticket) dequantises and re-zeroes it.
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -31,7 +37,6 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage
-constexpr int kEpiWarp0 = 2;
 constexpr int kThreads = 192;
 // Split-K tickets live in a fixed region at the start of the workspace so
 // that calls of different shapes sharing one buffer find them at zero.
@@ -40,18 +45,12 @@ constexpr size_t kTicketBytes = 64 * 1024;
 struct GemmParams {
   int64_t M, N, K, ldc;
   int k_tiles;          // ceil(K / BK)
-  int k_tiles_split;    // k tiles per split
+  int k_tiles_split;    // k tiles per split (skinny)
   int splits;
   int stages;
-  int out_dtype;
+  int m_tiles, n_tiles, num_tiles;
   uint32_t stage_bytes;
-};
-
-template <int BN>
-struct Smem {
-  static constexpr uint32_t kA = BM * BK;  // 16 KB
-  static constexpr uint32_t kB = BN * BK;
-  static constexpr uint32_t kStage = kA + kB;
+  uint32_t a_bytes;     // bytes of the first operand box in a stage
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -70,11 +69,18 @@ __device__ __forceinline__ void store_out_row(OutT* dst, const float* v, int n_v
         reinterpret_cast<float4*>(dst)[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
     }
   } else {
-    for (int j = 0; j < n_valid; ++j) dst[j] = from_f32<OutT>(v[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n_valid) dst[j] = from_f32<OutT>(v[j]);
   }
 }
 
-// Dequantises 32 accumulators of one row and writes them.
+__device__ __forceinline__ float dequant(uint32_t acc, float sa, float sw) {
+  return __fmul_rn(__fmul_rn(__int2float_rn((int)acc), sa), sw);
+}
+
+// Dequantises 32 accumulators of one row and writes them (and the raw
+// accumulators when acc_out is given).
 template <typename OutT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row, int64_t col0,
                                                const float* __restrict__ sA,
@@ -88,11 +94,10 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row,
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float sw = (j < n_valid) ? __ldg(&sW[col0 + j]) : 0.f;
-    v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j]), sa), sw);
+    v[j] = dequant(acc[j], sa, sw);
   }
   OutT* dst = C + row * p.ldc + col0;
-  const bool vec_ok = ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
-  store_out_row<OutT>(dst, v, n_valid, vec_ok);
+  store_out_row<OutT>(dst, v, n_valid, (reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
   if (acc_out != nullptr) {
     int32_t* ad = acc_out + row * p.N + col0;
     if (n_valid == 32 && ((reinterpret_cast<uintptr_t>(ad) & 15u) == 0)) {
@@ -100,182 +105,299 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row,
       for (int c = 0; c < 8; ++c)
         reinterpret_cast<int4*>(ad)[c] = make_int4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
     } else {
-      for (int j = 0; j < n_valid; ++j) ad[j] = (int32_t)acc[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < n_valid) ad[j] = (int32_t)acc[j];
     }
   }
 }
 
+// Shared-memory carve-up of both kernels: [ring of stages][barriers...]
+struct Bars {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* acc_full;   // [2]
+  uint64_t* acc_empty;  // [2]
+  uint64_t* mma_done;
+  uint32_t* tmem_slot;
+  int* flags;  // [0] abort, [1] last split
+};
+
+__device__ __forceinline__ Bars carve(uint8_t* smem, const GemmParams& p) {
+  Bars b;
+  b.full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  b.empty = b.full + p.stages;
+  b.acc_full = b.empty + p.stages;
+  b.acc_empty = b.acc_full + 2;
+  b.mma_done = b.acc_empty + 2;
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.mma_done + 1);
+  b.flags = reinterpret_cast<int*>(b.tmem_slot + 1);
+  return b;
+}
+
+__device__ __forceinline__ bool aborted(const Bars& b) { return *(volatile int*)&b.flags[0] != 0; }
+__device__ __forceinline__ void set_abort(const Bars& b, int code) {
+  b200_dev_error(code);
+  atomicExch(&b.flags[0], 1);
+}
+
+// Producer: streams `count` stages of {first operand box at (kx, r0), second
+// at (kx, r1)} for k tiles [kt0, kt0 + count), continuing the ring position
+// `it`.  Returns false if a wait timed out.
+__device__ __forceinline__ bool produce(const CUtensorMap* ta, const CUtensorMap* tb, const Bars& bars,
+                                        uint32_t base, const GemmParams& p, int kt0, int count, int32_t r0,
+                                        int32_t r1, int& it) {
+  for (int i = 0; i < count; ++i, ++it) {
+    const int s = it % p.stages;
+    if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[s]), ((it / p.stages) & 1) ^ 1)) return false;
+    if (aborted(bars)) return false;
+    const uint32_t fb = sm100::smem_u32(&bars.full[s]);
+    sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
+    const int32_t kx = (kt0 + i) * BK;
+    const uint32_t dst = base + s * p.stage_bytes;
+    sm100::tma_load_2d(dst, ta, fb, kx, r0);
+    sm100::tma_load_2d(dst + p.a_bytes, tb, fb, kx, r1);
+  }
+  return true;
+}
+
+// Waits (bounded) for the last fill of every stage so no bulk copy is still
+// landing when the CTA exits.
+__device__ __forceinline__ void drain_fills(const Bars& bars, const GemmParams& p, int it) {
+  for (int i = it - 1; i >= 0 && i >= it - p.stages; --i)
+    if (!sm100::mbar_wait(sm100::smem_u32(&bars.full[i % p.stages]), (i / p.stages) & 1))
+      b200_dev_error(kDevErrTimeoutFull);
+}
+
+// MMA issue of `count` stages into accumulator `d_tmem`; returns false on timeout.
+template <int N_MMA>
+__device__ __forceinline__ bool mma_stages(const Bars& bars, uint32_t base, const GemmParams& p, uint32_t d_tmem,
+                                           int count, int& it) {
+  constexpr uint32_t idesc = sm100::make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, 0, 0, BM, N_MMA);
+  for (int i = 0; i < count; ++i, ++it) {
+    const int s = it % p.stages;
+    if (!sm100::mbar_wait(sm100::smem_u32(&bars.full[s]), (it / p.stages) & 1)) return false;
+    if (aborted(bars)) return false;
+    sm100::tc_fence_after();
+    const uint32_t a_base = base + s * p.stage_bytes;
+    const uint32_t b_base = a_base + p.a_bytes;
+#pragma unroll
+    for (int kk = 0; kk < BK / 32; ++kk) {
+      // K-major SWIZZLE_128B: 8-row atoms of 1024 B stacked along M/N
+      // (SBO = 1024); stepping K by 32 bytes inside the atom moves the start
+      // address, the hardware applies the swizzle.
+      const uint64_t ad = sm100::make_smem_desc(a_base + kk * 32, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t bd = sm100::make_smem_desc(b_base + kk * 32, 16, 1024, sm100::kSwizzle128B);
+      sm100::mma_i8_ss(d_tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+    }
+    sm100::tc_commit(sm100::smem_u32(&bars.empty[s]));
+  }
+  return true;
+}
+
+__device__ __forceinline__ void init_bars(const Bars& bars, const GemmParams& p) {
+  for (int s = 0; s < p.stages; ++s) {
+    sm100::mbar_init(sm100::smem_u32(&bars.full[s]), 1);
+    sm100::mbar_init(sm100::smem_u32(&bars.empty[s]), 1);
+  }
+  for (int a = 0; a < 2; ++a) {
+    sm100::mbar_init(sm100::smem_u32(&bars.acc_full[a]), 1);
+    sm100::mbar_init(sm100::smem_u32(&bars.acc_empty[a]), 4);  // one arrival per epilogue warp
+  }
+  sm100::mbar_init(sm100::smem_u32(bars.mma_done), 1);
+  bars.flags[0] = 0;
+  bars.flags[1] = 0;
+  sm100::fence_barrier_init();
+}
+
+// ----------------------------------------------------------------------------
+// Persistent kernel (M > 64)
+// ----------------------------------------------------------------------------
 template <int BN, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
-    int8_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_a,
-                             const __grid_constant__ CUtensorMap tm_b, const float* __restrict__ sA,
-                             const float* __restrict__ sW, OutT* __restrict__ C,
-                             int32_t* __restrict__ acc_out, int32_t* __restrict__ partials,
-                             int* __restrict__ tickets, GemmParams p) {
+    int8_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                             const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
+                             int32_t* __restrict__ acc_out, GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the SWIZZLE_128B atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
-  const int64_t m0 = (int64_t)m_tile * BM, n0 = (int64_t)n_tile * BN;
-  const int kt0 = split * p.k_tiles_split;
-  const int kt1 = min(kt0 + p.k_tiles_split, p.k_tiles);
-  const int n_k = max(kt1 - kt0, 0);
-
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
-  uint64_t* empty_bar = full_bar + p.stages;
-  uint64_t* accum_bar = empty_bar + p.stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
-  int* s_flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last split
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      sm100::mbar_init(sm100::smem_u32(&full_bar[s]), 1);
-      sm100::mbar_init(sm100::smem_u32(&empty_bar[s]), 1);
-    }
-    sm100::mbar_init(sm100::smem_u32(accum_bar), 1);
-    s_flags[0] = 0;
-    s_flags[1] = 0;
-    sm100::fence_barrier_init();
-  }
+  const Bars bars = carve(smem, p);
+  const uint32_t base = sm100::smem_u32(smem);
+  if (threadIdx.x == 0) init_bars(bars, p);
   if (warp == 1) {
-    sm100::tmem_alloc(sm100::smem_u32(tmem_slot), BN);
+    sm100::tmem_alloc(sm100::smem_u32(bars.tmem_slot), 2 * BN);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *bars.tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
     if (lane == 0) {
       sm100::tma_prefetch_desc(&tm_a);
       sm100::tma_prefetch_desc(&tm_b);
-      const uint32_t base = sm100::smem_u32(smem);
-      int issued = 0;
-      for (int i = 0; i < n_k; ++i) {
-        const int s = i % p.stages;
-        if (!sm100::mbar_wait(sm100::smem_u32(&empty_bar[s]), ((i / p.stages) & 1) ^ 1)) {
-          b200_dev_error(kDevErrTimeoutEmpty);
-          atomicExch(&s_flags[0], 1);
+      int it = 0;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
+        if (!produce(&tm_a, &tm_b, bars, base, p, 0, p.k_tiles, m_tile * BM, n_tile * BN, it)) {
+          set_abort(bars, kDevErrTimeoutEmpty);
           break;
         }
-        if (*(volatile int*)&s_flags[0]) break;
-        const uint32_t fb = sm100::smem_u32(&full_bar[s]);
-        sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
-        const int32_t kx = (kt0 + i) * BK;
-        const uint32_t sa = base + s * p.stage_bytes;
-        sm100::tma_load_2d(sa, &tm_a, fb, kx, (int32_t)m0);
-        sm100::tma_load_2d(sa + Smem<BN>::kA, &tm_b, fb, kx, (int32_t)n0);
-        ++issued;
       }
-      for (int i = issued - 1; i >= 0 && i >= issued - p.stages; --i) {
-        const int s = i % p.stages;
-        if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1))
-          b200_dev_error(kDevErrTimeoutFull);
-      }
+      drain_fills(bars, p, it);
     }
   } else if (warp == 1) {
-    // ----------------------------------------------------------- MMA issue
     if (lane == 0) {
-      constexpr uint32_t idesc = sm100::make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, 0, 0, BM, BN);
-      const uint32_t base = sm100::smem_u32(smem);
-      for (int i = 0; i < n_k; ++i) {
-        const int s = i % p.stages;
-        if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
-          b200_dev_error(kDevErrTimeoutFull);
-          atomicExch(&s_flags[0], 1);
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++lt) {
+        const int a = lt & 1;
+        // the epilogue must have drained this accumulator (tile lt - 2)
+        if (!sm100::mbar_wait(sm100::smem_u32(&bars.acc_empty[a]), ((lt >> 1) & 1) ^ 1)) {
+          ok = false;
           break;
         }
-        if (*(volatile int*)&s_flags[0]) break;
         sm100::tc_fence_after();
-        const uint32_t a_base = base + s * p.stage_bytes;
-        const uint32_t b_base = a_base + Smem<BN>::kA;
-#pragma unroll
-        for (int kk = 0; kk < BK / 32; ++kk) {
-          // K-major SWIZZLE_128B: 8-row atoms of 1024 B stacked along M/N
-          // (SBO = 1024); stepping K by 32 bytes inside the atom moves the
-          // start address, the hardware applies the swizzle.
-          const uint64_t ad = sm100::make_smem_desc(a_base + kk * 32, 16, 1024, sm100::kSwizzle128B);
-          const uint64_t bd = sm100::make_smem_desc(b_base + kk * 32, 16, 1024, sm100::kSwizzle128B);
-          sm100::mma_i8_ss(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        sm100::tc_commit(sm100::smem_u32(&empty_bar[s]));
+        ok = mma_stages<BN>(bars, base, p, tmem + a * BN, p.k_tiles, it);
+        sm100::tc_commit(sm100::smem_u32(&bars.acc_full[a]));
       }
-      // Signals the epilogue once every issued MMA has completed (also on
-      // the abort path, so TMEM is never released under a running MMA).
-      sm100::tc_commit(sm100::smem_u32(accum_bar));
+      if (!ok) set_abort(bars, kDevErrTimeoutFull);
+      // every issued MMA has completed before TMEM is released
+      sm100::tc_commit(sm100::smem_u32(bars.mma_done));
+      if (!sm100::mbar_wait(sm100::smem_u32(bars.mma_done), 0)) b200_dev_error(kDevErrTimeoutMma);
     }
   } else {
-    // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    const int64_t row = m0 + quarter * 32 + lane;
-    const bool ok = sm100::mbar_wait(sm100::smem_u32(accum_bar), 0);
-    if (!ok) {
-      b200_dev_error(kDevErrTimeoutMma);
-      atomicExch(&s_flags[0], 1);
-    }
-    sm100::tc_fence_after();
-    const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16);
-    if (p.splits == 1) {
-      if (ok) {
+    int lt = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++lt) {
+      const int a = lt & 1;
+      if (!sm100::mbar_wait(sm100::smem_u32(&bars.acc_full[a]), (lt >> 1) & 1)) {
+        set_abort(bars, kDevErrTimeoutMma);
+        break;
+      }
+      sm100::tc_fence_after();
+      const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
+      const int64_t row = (int64_t)m_tile * BM + quarter * 32 + lane;
+      const uint32_t t_row = tmem + a * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t acc[32];
-          sm100::tmem_ld_32x32b_x32(t_row + c, acc);
-          sm100::tmem_wait_ld();
-          if (n_k == 0) {
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t acc[32];
+        sm100::tmem_ld_32x32b_x32(t_row + c, acc);
+        sm100::tmem_wait_ld();
+        if (row < p.M && !aborted(bars))
+          epilogue_chunk<OutT>(acc, row, (int64_t)n_tile * BN + c, sA, sW, C, acc_out, p);
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&bars.acc_empty[a]));
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Skinny kernel (M <= 64): C^T tiles [128 n x MN m], split-K
+// ----------------------------------------------------------------------------
+template <int MN, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    int8_gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                            const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
+                            int32_t* __restrict__ acc_out, int32_t* __restrict__ ws, int* __restrict__ tickets,
+                            GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Bars bars = carve(smem, p);
+  const uint32_t base = sm100::smem_u32(smem);
+  constexpr int kCols = MN < 32 ? 32 : MN;  // TMEM allocation granularity
+  const int n_tile = blockIdx.x, split = blockIdx.y;
+  const int kt0 = split * p.k_tiles_split;
+  const int nk = max(0, min(p.k_tiles, kt0 + p.k_tiles_split) - kt0);
+  if (threadIdx.x == 0) init_bars(bars, p);
+  if (warp == 1) {
+    sm100::tmem_alloc(sm100::smem_u32(bars.tmem_slot), kCols);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *bars.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_w);
+      sm100::tma_prefetch_desc(&tm_a);
+      int it = 0;
+      if (!produce(&tm_w, &tm_a, bars, base, p, kt0, nk, n_tile * BM, 0, it)) set_abort(bars, kDevErrTimeoutEmpty);
+      drain_fills(bars, p, it);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0;
+      if (!mma_stages<MN>(bars, base, p, tmem, nk, it)) set_abort(bars, kDevErrTimeoutFull);
+      sm100::tc_commit(sm100::smem_u32(&bars.acc_full[0]));
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
+    const bool ok = sm100::mbar_wait(sm100::smem_u32(&bars.acc_full[0]), 0);
+    if (!ok) set_abort(bars, kDevErrTimeoutMma);
+    sm100::tc_fence_after();
+    uint32_t acc[MN];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = 0;
+    for (int c = 0; c < MN; c += 16)
+      sm100::tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + c, acc + c);
+    sm100::tmem_wait_ld();
+    if (nk == 0) {
+#pragma unroll
+      for (int j = 0; j < MN; ++j) acc[j] = 0;
+    }
+    const bool n_ok = n < p.N && ok && !aborted(bars);
+    if (p.splits == 1) {
+      if (n_ok) {
+        const float sw = sW[n];
+#pragma unroll
+        for (int m = 0; m < MN; ++m) {
+          if (m < p.M) {
+            C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant(acc[m], sA[m], sw));
+            if (acc_out) acc_out[(int64_t)m * p.N + n] = (int32_t)acc[m];
           }
-          if (row < p.M) epilogue_chunk<OutT>(acc, row, n0 + c, sA, sW, C, acc_out, p);
         }
       }
     } else {
-      // write this split's partial tile, then the last split reduces
-      const int64_t Mp = (int64_t)gridDim.x * BM;
-      int32_t* mine = partials + ((int64_t)split * Mp + row) * p.N;
-      if (ok) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t acc[32];
-          sm100::tmem_ld_32x32b_x32(t_row + c, acc);
-          sm100::tmem_wait_ld();
-          if (n_k == 0) {
+      // exact int32 partial sums: red.add into the tile, ticket, last split finishes
+      if (n_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = 0;
-          }
-          const int64_t col0 = n0 + c;
-          if (row < p.M)
-            for (int j = 0; j < 32 && col0 + j < p.N; ++j) mine[col0 + j] = (int32_t)acc[j];
-        }
+        for (int m = 0; m < MN; ++m)
+          if (m < p.M) atomicAdd(&ws[(int64_t)m * p.N + n], (int)acc[m]);
       }
       __threadfence();
       named_bar_sync(1, 128);
-      if (threadIdx.x == kEpiWarp0 * 32) {
-        int* t = tickets + (int64_t)m_tile * gridDim.y + n_tile;
-        const int prev = atomicAdd(t, 1);
+      if (threadIdx.x == 2 * 32) {
+        const int prev = atomicAdd(&tickets[n_tile], 1);
         const int last = (prev == p.splits - 1);
-        if (last) atomicExch(t, 0);
-        s_flags[1] = last;
+        if (last) atomicExch(&tickets[n_tile], 0);
+        bars.flags[1] = last;
       }
       named_bar_sync(1, 128);
-      if (s_flags[1]) {
+      if (bars.flags[1]) {
         __threadfence();
-        if (row < p.M) {
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            const int64_t col0 = n0 + c;
-            if (col0 >= p.N) break;
-            uint32_t acc[32];
+        if (n_ok) {
+          const float sw = sW[n];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = 0;
-            for (int s = 0; s < p.splits; ++s) {
-              const int32_t* src = partials + ((int64_t)s * Mp + row) * p.N + col0;
-              for (int j = 0; j < 32 && col0 + j < p.N; ++j) acc[j] += (uint32_t)__ldcg(src + j);
+          for (int m = 0; m < MN; ++m) {
+            if (m < p.M) {
+              int32_t* cell = &ws[(int64_t)m * p.N + n];
+              const int32_t v = __ldcg(cell);
+              *cell = 0;  // ready for the next call
+              C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant((uint32_t)v, sA[m], sw));
+              if (acc_out) acc_out[(int64_t)m * p.N + n] = v;
             }
-            epilogue_chunk<OutT>(acc, row, col0, sA, sW, C, acc_out, p);
           }
         }
       }
@@ -285,67 +407,83 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, BN);
+    sm100::tmem_dealloc(tmem, kCols);
   }
 }
 
 struct GemmPlan {
-  int BN, splits, k_tiles, k_tiles_split, stages;
-  uint32_t stage_bytes;
+  bool skinny;
+  int BN;  // persistent tile width, or MN (padded M) for skinny
+  int splits, k_tiles, k_tiles_split, stages, m_tiles, n_tiles, grid;
+  uint32_t stage_bytes, a_bytes;
   size_t smem, ws_bytes;
-  int m_tiles, n_tiles;
 };
 
 GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) {
   GemmPlan g{};
   g.k_tiles = (int)((K + BK - 1) / BK);
   const int sms = device_sm_count();
-  int bn = (cfg && cfg->tile_n > 0) ? cfg->tile_n : 0;
-  g.m_tiles = (int)((M + BM - 1) / BM);
-  if (bn != 128 && bn != 256) {
-    // 256-wide tiles when they still give at least one full wave of CTAs.
-    const int64_t t256 = g.m_tiles * ((N + 255) / 256);
-    bn = (t256 >= sms && N >= 256) ? 256 : 128;
-  }
-  g.BN = bn;
-  g.n_tiles = (int)((N + bn - 1) / bn);
-  int splits = (cfg && cfg->split > 0) ? cfg->split : 0;
-  if (splits == 0) {
-    const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
-    splits = 1;
-    while (tiles * splits < sms && splits * 2 <= g.k_tiles && splits < 16) splits *= 2;
-  }
-  if (splits > g.k_tiles) splits = g.k_tiles;
-  if (splits < 1) splits = 1;
-  g.k_tiles_split = (g.k_tiles + splits - 1) / splits;
-  g.splits = (g.k_tiles + g.k_tiles_split - 1) / g.k_tiles_split;
-  g.stage_bytes = (uint32_t)(BM * BK + bn * BK);
   const size_t budget = 227 * 1024 - 1024 - 256;
+  g.skinny = M <= 64 && !(cfg && (cfg->flags & 1));  // flags bit 0: force the persistent kernel
+  if (g.skinny) {
+    g.BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    g.m_tiles = 1;
+    g.n_tiles = (int)((N + BM - 1) / BM);
+    int splits = (cfg && cfg->split > 0) ? cfg->split : 0;
+    if (splits == 0) {
+      splits = 1;
+      while (g.n_tiles * splits < sms && splits * 2 <= g.k_tiles) splits *= 2;
+    }
+    if (splits > g.k_tiles) splits = g.k_tiles;
+    g.k_tiles_split = (g.k_tiles + splits - 1) / splits;
+    g.splits = (g.k_tiles + g.k_tiles_split - 1) / g.k_tiles_split;
+    g.a_bytes = BM * BK;  // W box
+    g.stage_bytes = g.a_bytes + g.BN * BK;
+    g.grid = g.n_tiles * g.splits;
+    if (g.splits > 1) g.ws_bytes = kTicketBytes + (size_t)M * N * 4;
+  } else {
+    int bn = (cfg && cfg->tile_n > 0) ? cfg->tile_n : 256;
+    if (bn != 128 && bn != 256) bn = 256;
+    if (N <= 128) bn = 128;
+    g.BN = bn;
+    g.m_tiles = (int)((M + BM - 1) / BM);
+    g.n_tiles = (int)((N + bn - 1) / bn);
+    g.splits = 1;
+    g.k_tiles_split = g.k_tiles;
+    g.a_bytes = BM * BK;
+    g.stage_bytes = g.a_bytes + bn * BK;
+    const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
+    g.grid = (int)(tiles < sms ? tiles : sms);
+  }
   int stages = (cfg && cfg->stages > 0) ? cfg->stages : 8;
   while (stages > 2 && (size_t)stages * g.stage_bytes > budget) --stages;
   g.stages = stages;
   g.smem = (size_t)stages * g.stage_bytes + 1024 + 256;
-  if (g.splits > 1) {
-    const size_t parts = (size_t)g.splits * g.m_tiles * BM * (size_t)N * 4;
-    g.ws_bytes = kTicketBytes + parts;
-  }
   return g;
 }
 
-template <int BN, typename OutT>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
-                int32_t* acc_out, void* ws, const GemmPlan& g, GemmParams p, cudaStream_t s) {
-  auto kern = int8_gemm_tcgen05_kernel<BN, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+template <typename OutT>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
+           int32_t* acc_out, void* ws, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
+  if (!g.skinny) {
+    auto kern = g.BN == 256 ? int8_gemm_tcgen05_kernel<256, OutT> : int8_gemm_tcgen05_kernel<128, OutT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+    if (e != cudaSuccess) return launch_status(e);
+    kern<<<g.grid, kThreads, g.smem, s>>>(ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, p);
+    return launch_status(cudaGetLastError());
+  }
+  auto sk = g.BN == 16 ? int8_gemm_skinny_kernel<16, OutT>
+                       : (g.BN == 32 ? int8_gemm_skinny_kernel<32, OutT> : int8_gemm_skinny_kernel<64, OutT>);
+  cudaError_t e = cudaFuncSetAttribute(sk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
   if (e != cudaSuccess) return launch_status(e);
-  int32_t* parts = nullptr;
   int* tickets = nullptr;
+  int32_t* part = nullptr;
   if (g.splits > 1) {
     tickets = static_cast<int*>(ws);
-    parts = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + kTicketBytes);
+    part = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + kTicketBytes);
   }
-  dim3 grid(g.m_tiles, g.n_tiles, g.splits);
-  kern<<<grid, kThreads, g.smem, s>>>(ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, parts, tickets, p);
+  dim3 grid(g.n_tiles, g.splits);
+  sk<<<grid, kThreads, g.smem, s>>>(ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, part, tickets, p);
   return launch_status(cudaGetLastError());
 }
 
@@ -373,23 +511,30 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
   if (!aligned16(A) || !aligned16(W)) return B200_ERR_ALIGNMENT;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
   const GemmPlan g = plan_gemm(M, N, K, cfg);
-  if (g.m_tiles > 65535 * 1024 || g.n_tiles > 65535) return B200_ERR_UNSUPPORTED;
-  if (g.splits > 1 && (workspace == nullptr || workspace_bytes < g.ws_bytes)) return B200_ERR_WORKSPACE;
-  if (g.splits > 1 && (size_t)g.m_tiles * g.n_tiles * 4 > kTicketBytes) return B200_ERR_UNSUPPORTED;
+  if (g.skinny && g.splits > 1) {
+    if (workspace == nullptr || workspace_bytes < g.ws_bytes || !aligned16(workspace)) return B200_ERR_WORKSPACE;
+    if ((size_t)g.n_tiles * 4 > kTicketBytes) return B200_ERR_UNSUPPORTED;
+  }
+  if (g.skinny && g.n_tiles > 0x7fffffff / 2) return B200_ERR_UNSUPPORTED;
+  // first MMA operand: A (persistent) or W (skinny: operands swapped)
   CUtensorMap ta, tb;
+  const int8_t* op0 = g.skinny ? W : A;
+  const int8_t* op1 = g.skinny ? A : W;
+  const int64_t rows0 = g.skinny ? N : M;
+  const int64_t rows1 = g.skinny ? M : N;
   {
-    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)rows0};
     const uint64_t strides[1] = {(uint64_t)K};
     const uint32_t box[2] = {BK, BM};
-    int st = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, A, dims, strides, box,
+    int st = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, op0, dims, strides, box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
   {
-    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)rows1};
     const uint64_t strides[1] = {(uint64_t)K};
     const uint32_t box[2] = {BK, (uint32_t)g.BN};
-    int st = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W, dims, strides, box,
+    int st = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, op1, dims, strides, box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
@@ -402,18 +547,16 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
   p.k_tiles_split = g.k_tiles_split;
   p.splits = g.splits;
   p.stages = g.stages;
-  p.out_dtype = out_dtype;
+  p.m_tiles = g.m_tiles;
+  p.n_tiles = g.n_tiles;
+  p.num_tiles = g.m_tiles * g.n_tiles;
   p.stage_bytes = g.stage_bytes;
+  p.a_bytes = g.a_bytes;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto go = [&](auto out_tag) -> int {
-    using OutT = decltype(out_tag);
-    return g.BN == 256 ? launch_gemm<256, OutT>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s)
-                       : launch_gemm<128, OutT>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
-  };
   switch (out_dtype) {
-    case B200_F16: return go(__half{});
-    case B200_BF16: return go(__nv_bfloat16{});
-    case B200_F32: return go(float{});
+    case B200_F16: return launch<__half>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
+    case B200_BF16: return launch<__nv_bfloat16>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
+    case B200_F32: return launch<float>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
     default: return B200_ERR_UNSUPPORTED;
   }
 }

@@ -54,6 +54,10 @@ struct DecodeParams {
   float qscale;          // scale * log2(e)
 };
 
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -143,6 +147,88 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int ntok) {
   return v & (lo | hi);
 }
 
+// One page (ntok tokens of one kv head, K tile at kb, V tile at vb in the
+// swizzled [d-half][head][token][64] layout) folded into the running
+// (o, m_used, l_part) of this warp's query heads.
+template <typename T>
+__device__ __forceinline__ void mma_page(uint32_t kb, uint32_t vb, int ntok, int w, int bs, int lane,
+                                         uint32_t hbytes, float sl2, const uint32_t (&qa)[8][2],
+                                         float (&o)[16][4], float& m_used, float& l_part) {
+  const int qc = (lane & 3) * 2;
+  const int mat = lane >> 3, mrow = lane & 7;
+  for (int t0 = 0; t0 < ntok; t0 += 16) {
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    {
+      // lane supplies row `mrow` of matrix `mat`: (n-tile mat>>1, d-chunk parity mat&1)
+      const int row = w * bs + t0 + (mat >> 1) * 8 + mrow;
+      const uint32_t rbase = kb + row * 128;
+      const int sw = row & 7;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int chunk = ((ks & 3) << 1) | (mat & 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(rbase + (ks >> 2) * hbytes + ((chunk ^ sw) << 4), b00, b01, b10, b11);
+        mma16816<T>(sc[0], qa[ks][0], qa[ks][1], b00, b01);
+        mma16816<T>(sc[1], qa[ks][0], qa[ks][1], b10, b11);
+      }
+    }
+    float x[4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = t0 + nt * 8 + qc + e;
+        x[nt * 2 + e] = tok < ntok ? sc[nt][e] * sl2 : -INFINITY;
+      }
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (m_used == -INFINITY) {
+      m_used = mx;
+    } else if (mx > m_used + 8.0f) {
+      const float alpha = exp2f(m_used - mx);
+      m_used = mx;
+      l_part *= alpha;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= alpha;
+        o[j][1] *= alpha;
+      }
+    }
+    float pv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      pv[j] = exp2f(x[j] - m_used);
+      l_part += pv[j];
+    }
+    const uint32_t pa0 = pack_pair<T>(pv[0], pv[1]);  // tokens qc+{0,1}
+    const uint32_t pa2 = pack_pair<T>(pv[2], pv[3]);  // tokens 8+qc+{0,1}
+    const bool partial = (t0 + 16 > ntok);
+    {
+      // matrix `mat`: token half mat&1, d-chunk offset mat>>1
+      const int row = w * bs + t0 + (mat & 1) * 8 + mrow;
+      const uint32_t rbase = vb + row * 128;
+      const int sw = row & 7;
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        const int d0 = np * 16 + (mat >> 1) * 8;
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(rbase + (d0 >> 6) * hbytes + ((((d0 & 63) >> 3) ^ sw) << 4), v0, v1, v2, v3);
+        if (partial) {
+          v0 = mask_pair(v0, t0 + qc, ntok);
+          v1 = mask_pair(v1, t0 + 8 + qc, ntok);
+          v2 = mask_pair(v2, t0 + qc, ntok);
+          v3 = mask_pair(v3, t0 + 8 + qc, ntok);
+        }
+        mma16816<T>(o[2 * np], pa0, pa2, v0, v1);
+        mma16816<T>(o[2 * np + 1], pa0, pa2, v2, v3);
+      }
+    }
+  }
+}
+
 template <typename T, int G>
 __device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
                                             const int* list_ntok, int* s_misc, int npages, int nsplit,
@@ -171,7 +257,6 @@ __device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, u
   const float sl2 = p.qscale;
   const uint32_t base = sm100::smem_u32(smem);
   const uint32_t hbytes = p.stage_bytes / 4;
-  const int mat = lane >> 3, mrow = lane & 7;
 
   for (int i = 0; i < npages; ++i) {
     const int s = i % p.stages;
@@ -184,77 +269,7 @@ __device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, u
     const int ntok = list_ntok[i];
     const uint32_t kb = base + s * p.stage_bytes;
     const uint32_t vb = kb + 2 * hbytes;
-    for (int t0 = 0; t0 < ntok; t0 += 16) {
-      float sc[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-      {
-        // lane supplies row `mrow` of matrix `mat`: (n-tile mat>>1, d-chunk parity mat&1)
-        const int row = w * bs + t0 + (mat >> 1) * 8 + mrow;
-        const uint32_t rbase = kb + row * 128;
-        const int sw = row & 7;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const int chunk = ((ks & 3) << 1) | (mat & 1);
-          uint32_t b00, b01, b10, b11;
-          ldsm_x4(rbase + (ks >> 2) * hbytes + ((chunk ^ sw) << 4), b00, b01, b10, b11);
-          mma16816<T>(sc[0], qa[ks][0], qa[ks][1], b00, b01);
-          mma16816<T>(sc[1], qa[ks][0], qa[ks][1], b10, b11);
-        }
-      }
-      float x[4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int tok = t0 + nt * 8 + qc + e;
-          x[nt * 2 + e] = tok < ntok ? sc[nt][e] * sl2 : -INFINITY;
-        }
-      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      if (m_used == -INFINITY) {
-        m_used = mx;
-      } else if (mx > m_used + 8.0f) {
-        const float alpha = exp2f(m_used - mx);
-        m_used = mx;
-        l_part *= alpha;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          o[j][0] *= alpha;
-          o[j][1] *= alpha;
-        }
-      }
-      float pv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        pv[j] = exp2f(x[j] - m_used);
-        l_part += pv[j];
-      }
-      const uint32_t pa0 = pack_pair<T>(pv[0], pv[1]);  // tokens qc+{0,1}
-      const uint32_t pa2 = pack_pair<T>(pv[2], pv[3]);  // tokens 8+qc+{0,1}
-      const bool partial = (t0 + 16 > ntok);
-      {
-        // matrix `mat`: token half mat&1, d-chunk offset mat>>1
-        const int row = w * bs + t0 + (mat & 1) * 8 + mrow;
-        const uint32_t rbase = vb + row * 128;
-        const int sw = row & 7;
-#pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          const int d0 = np * 16 + (mat >> 1) * 8;
-          uint32_t v0, v1, v2, v3;
-          ldsm_x4_t(rbase + (d0 >> 6) * hbytes + ((((d0 & 63) >> 3) ^ sw) << 4), v0, v1, v2, v3);
-          if (partial) {
-            v0 = mask_pair(v0, t0 + qc, ntok);
-            v1 = mask_pair(v1, t0 + 8 + qc, ntok);
-            v2 = mask_pair(v2, t0 + qc, ntok);
-            v3 = mask_pair(v3, t0 + 8 + qc, ntok);
-          }
-          mma16816<T>(o[2 * np], pa0, pa2, v0, v1);
-          mma16816<T>(o[2 * np + 1], pa0, pa2, v2, v3);
-        }
-      }
-    }
+    mma_page<T>(kb, vb, ntok, w, bs, lane, hbytes, sl2, qa, o, m_used, l_part);
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&empty_bar[s]));
   }
@@ -707,9 +722,365 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent flat-partition decode (tensor-core consumer).
+//
+// All sequences' block-table entries are laid end to end (segment s = hg*B + b
+// holds ceil(ctx_b / bs) entries) and the grid's CTAs -- one per SM -- take
+// equal contiguous ranges of that list, so every SM streams the same number
+// of KV pages whatever the context lengths are.  The producer warp walks its
+// range segment by segment without draining the TMA ring: each stage carries
+// a small PageMeta record, either a data page (ntok surviving tokens) or an
+// end-of-segment marker.  On a marker the consumer warps finish the segment:
+// a segment wholly inside this CTA's range is written directly; otherwise the
+// CTA writes its (m, l, o) piece to one of its two partial slots (slot 0 for
+// the first segment of its range, 1 for the last) and the CTA that finishes
+// the segment's last piece (atomic ticket) merges the pieces.  Per segment,
+// the token rank rule of the reference (dropped ids shift later blocks) is
+// applied exactly as in the split kernel.
+// ---------------------------------------------------------------------------
+constexpr int kFlatMaxSeg = 1024;
+
+struct FlatParams {
+  int64_t B, Hq, Hkv, num_blocks, block_size, max_blocks;
+  int HG, n_hg, stages, nseg;
+  uint32_t stage_bytes;
+  float qscale;
+};
+
+struct PageMeta {
+  int kind;     // 0 data page, 1 end of segment, 2 end of stream
+  int ntok;     // data: surviving tokens of the page
+  int seg;      // segment id hg * B + b
+  int slot;     // marker: partial slot of this CTA's piece, or -1 when direct
+  int c1, c2;   // marker: CTAs holding the segment's pieces
+  int c1_slot;  // marker: slot used by the piece of CTA c1
+  int pad;
+};
+
+__device__ __forceinline__ int64_t flat_lo(int64_t c, int64_t E, int64_t G) { return c * E / G; }
+__device__ __forceinline__ int flat_owner(int64_t e, int64_t E, int64_t G) {
+  return (int)(((e + 1) * G + E - 1) / E - 1);
+}
+
+template <typename T, typename IDX, int G>
+__global__ void __launch_bounds__(288, 1)
+    paged_decode_flat_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                             const T* __restrict__ q, const IDX* __restrict__ block_table,
+                             const IDX* __restrict__ ctx_len, T* __restrict__ out, float* __restrict__ ws_rows,
+                             int* __restrict__ tickets, FlatParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HG = p.HG;
+  const int heads_cta = HG * G;
+  const int64_t B = p.B;
+  const int bs = (int)p.block_size;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  uint64_t* empty_bar = full_bar + p.stages;
+  PageMeta* meta = reinterpret_cast<PageMeta*>(empty_bar + p.stages);
+  int64_t* s_cum = reinterpret_cast<int64_t*>(meta + p.stages);
+  int64_t* s_ctx = s_cum + (p.nseg + 1);
+  int* chunk_id = reinterpret_cast<int*>(s_ctx + B);
+  int* chunk_ntok = chunk_id + 32;
+  float* s_comb = reinterpret_cast<float*>(chunk_ntok + 32);  // [2][64]
+  int* s_flags = reinterpret_cast<int*>(s_comb + 128);        // [0] abort, [1] last piece
+
+  // ---- prologue: contexts, entry prefix over segments, barriers
+  if (warp == HG) {
+    for (int64_t b = lane; b < B; b += 32) s_ctx[b] = (int64_t)ctx_len[b];
+    __syncwarp();
+    int64_t run = 0;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    (void)lt_mask;
+    for (int s0 = 0; s0 < p.nseg; s0 += 32) {
+      const int s = s0 + lane;
+      int64_t e = 0;
+      if (s < p.nseg) {
+        const int64_t ctx = s_ctx[s % B];
+        const int64_t nvb = ctx > 0 ? (ctx + bs - 1) / bs : 0;
+        e = nvb < p.max_blocks ? nvb : p.max_blocks;
+      }
+      int64_t incl = e;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (s < p.nseg) s_cum[s + 1] = run + incl;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      s_cum[0] = 0;
+      s_flags[0] = 0;
+      s_flags[1] = 0;
+      for (int s = 0; s < p.stages; ++s) {
+        sm100::mbar_init(sm100::smem_u32(&full_bar[s]), 1);
+        sm100::mbar_init(sm100::smem_u32(&empty_bar[s]), HG);
+      }
+      sm100::fence_barrier_init();
+    }
+  }
+  __syncthreads();
+  const int64_t E = s_cum[p.nseg];
+  const int64_t Gc = gridDim.x;
+  const int64_t Geff = E < Gc ? E : Gc;
+  const int c = blockIdx.x;
+
+  // Segments without entries (context <= 0) are never streamed: zero them.
+  if (warp < HG) {
+    for (int s = c; s < p.nseg; s += (int)Gc) {
+      if (s_cum[s + 1] != s_cum[s]) continue;
+      const int64_t b = s % B, hg = s / B;
+      T* orow = out + (b * p.Hq + hg * heads_cta) * kD;
+      for (int i = threadIdx.x; i < heads_cta * kD; i += HG * 32) orow[i] = from_f32<T>(0.f);
+    }
+  }
+  if (c >= Geff) return;  // uniform per CTA
+  const int64_t lo = flat_lo(c, E, Geff), hi = flat_lo(c + 1, E, Geff);
+
+  if (warp == HG) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_k);
+      sm100::tma_prefetch_desc(&tm_v);
+    }
+    const uint32_t base = sm100::smem_u32(smem);
+    const uint32_t hb = p.stage_bytes / 4;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    int it = 0;
+    bool ok = true;
+    // lane 0 pushes one ring entry; returns false on timeout
+    auto push = [&](const PageMeta& m, int32_t tok0, int32_t h0) -> bool {
+      const int st = it % p.stages;
+      if (!sm100::mbar_wait(sm100::smem_u32(&empty_bar[st]), ((it / p.stages) & 1) ^ 1)) return false;
+      meta[st] = m;
+      const uint32_t fb = sm100::smem_u32(&full_bar[st]);
+      if (m.kind == 0) {
+        sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
+        const uint32_t dst = base + st * p.stage_bytes;
+        sm100::tma_load_3d(dst, &tm_k, fb, 0, tok0, h0);
+        sm100::tma_load_3d(dst + hb, &tm_k, fb, 64, tok0, h0);
+        sm100::tma_load_3d(dst + 2 * hb, &tm_v, fb, 0, tok0, h0);
+        sm100::tma_load_3d(dst + 3 * hb, &tm_v, fb, 64, tok0, h0);
+      } else {
+        sm100::mbar_arrive(fb);
+      }
+      ++it;
+      return true;
+    };
+    // segment containing lo: the largest s with cum[s] <= lo
+    int s = 0;
+    {
+      int l = 0, r = p.nseg;  // invariant cum[l] <= lo < cum[r]
+      while (r - l > 1) {
+        const int mid = (l + r) >> 1;
+        if (s_cum[mid] <= lo) l = mid;
+        else r = mid;
+      }
+      s = l;
+    }
+    int64_t e = lo;
+    bool first = true;
+    while (e < hi && ok) {
+      while (s_cum[s + 1] == s_cum[s]) ++s;
+      const int64_t b = s % B;
+      const int hg = s / (int)B;
+      const int64_t segs = s_cum[s], sege = s_cum[s + 1];
+      const int j0 = (int)(e - segs);
+      const int j1 = (int)((hi < sege ? hi : sege) - segs);
+      const int c1 = flat_owner(segs, E, Geff), c2 = flat_owner(sege - 1, E, Geff);
+      const int my_slot = first ? 0 : 1;
+      const int c1_slot = (segs == flat_lo(c1, E, Geff)) ? 0 : 1;
+      const int64_t ctx = s_ctx[b];
+      const IDX* bt = block_table + b * p.max_blocks;
+      // invalid entries before j0 shift the token ranks of this range
+      int inval = 0;
+      for (int jb = 0; jb < j0; jb += 256) {
+        IDX v[8];
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const int j = jb + rr * 32 + lane;
+          v[rr] = j < j0 ? __ldg(&bt[j]) : (IDX)0;
+        }
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) inval += (jb + rr * 32 + lane < j0 && bad_block(v[rr], p.num_blocks)) ? 1 : 0;
+      }
+      inval = __reduce_add_sync(0xffffffffu, inval);
+      for (int jj = j0; jj < j1 && ok; jj += 32) {
+        const int j = jj + lane;
+        const bool in = j < j1;
+        const IDX id = in ? __ldg(&bt[j]) : (IDX)-1;
+        const bool valid = in && !bad_block(id, p.num_blocks);
+        const unsigned ib = __ballot_sync(0xffffffffu, in && !valid);
+        const int64_t rank = (int64_t)j - (inval + __popc(ib & lt_mask));
+        int64_t nt = ctx - rank * bs;
+        nt = nt < 0 ? 0 : (nt > bs ? bs : nt);
+        const bool use = valid && nt > 0;
+        const unsigned ub = __ballot_sync(0xffffffffu, use);
+        if (use) {
+          const int k = __popc(ub & lt_mask);
+          chunk_id[k] = (int)id;
+          chunk_ntok[k] = (int)nt;
+        }
+        inval += __popc(ib);
+        __syncwarp();
+        if (lane == 0) {
+          const int n = __popc(ub);
+          for (int u = 0; u < n && ok; ++u) {
+            PageMeta m{0, chunk_ntok[u], s, 0, 0, 0, 0, 0};
+            ok = !(*(volatile int*)&s_flags[0]) && push(m, chunk_id[u] * bs, hg * HG);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();
+      }
+      if (lane == 0 && ok) {
+        PageMeta m{1, 0, s, c1 == c2 ? -1 : my_slot, c1, c2, c1_slot, 0};
+        ok = push(m, 0, 0);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      e = segs + j1;
+      if (e == sege) ++s;
+      first = false;
+    }
+    if (lane == 0) {
+      if (ok) {
+        PageMeta m{2, 0, 0, 0, 0, 0, 0, 0};
+        ok = push(m, 0, 0);
+      }
+      if (!ok) {
+        b200_dev_error(kDevErrTimeoutEmpty);
+        atomicExch(&s_flags[0], 1);
+      }
+      // never leave with bulk copies landing in shared memory
+      for (int i = it - 1; i >= 0 && i >= it - p.stages; --i)
+        if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[i % p.stages]), (i / p.stages) & 1))
+          b200_dev_error(kDevErrTimeoutFull);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int w = warp;
+  const int qh = lane >> 2, qc = (lane & 3) * 2;
+  const uint32_t base = sm100::smem_u32(smem);
+  const uint32_t hbytes = p.stage_bytes / 4;
+  uint32_t qa[8][2];
+  float o[16][4];
+  float m_used = -INFINITY, l_part = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  int cur_seg = -1;
+  const int nthr = HG * 32;
+  for (int it = 0;; ++it) {
+    const int st = it % p.stages;
+    if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[st]), (it / p.stages) & 1)) {
+      b200_dev_error(kDevErrTimeoutFull);
+      atomicExch(&s_flags[0], 1);
+      break;
+    }
+    const PageMeta m = meta[st];
+    if (m.kind == 0) {
+      if (m.seg != cur_seg) {
+        cur_seg = m.seg;
+        const int64_t b = m.seg % B, kvh = (int64_t)(m.seg / B) * HG + w;
+        const T* qr = q + (b * p.Hq + kvh * G + (qh < G ? qh : 0)) * kD;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          qa[ks][0] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + qc) : 0u;
+          qa[ks][1] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + qc) : 0u;
+        }
+      }
+      const uint32_t kb = base + st * p.stage_bytes;
+      mma_page<T>(kb, kb + 2 * hbytes, m.ntok, w, bs, lane, hbytes, p.qscale, qa, o, m_used, l_part);
+    } else if (m.kind == 1) {
+      // ---- finish segment m.seg
+      float l = l_part;
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      const int64_t b = m.seg % B, hg = m.seg / B;
+      const int64_t head = hg * heads_cta + w * G + qh;  // head index inside the sequence
+      if (m.slot < 0) {
+        if (qh < G) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          T* orow = out + (b * p.Hq + head) * kD;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            *reinterpret_cast<uint32_t*>(orow + 8 * j + qc) = pack_pair<T>(o[j][0] * inv, o[j][1] * inv);
+        }
+      } else {
+        if (qh < G) {
+          float* row = ws_rows + ((int64_t)(c * 2 + m.slot) * heads_cta + w * G + qh) * (kD + 2);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) *reinterpret_cast<float2*>(row + 8 * j + qc) = make_float2(o[j][0], o[j][1]);
+          if ((lane & 3) == 0) {
+            row[kD] = m_used;
+            row[kD + 1] = l;
+          }
+        }
+        __threadfence();
+        named_bar_sync(1, nthr);
+        if (threadIdx.x == 0) {
+          const int prev = atomicAdd(&tickets[m.seg], 1);
+          const int last = (prev == m.c2 - m.c1);
+          if (last) atomicExch(&tickets[m.seg], 0);
+          s_flags[1] = last;
+        }
+        named_bar_sync(1, nthr);
+        if (s_flags[1]) {
+          __threadfence();
+          for (int hh = threadIdx.x; hh < heads_cta; hh += nthr) {
+            float M = -INFINITY;
+            for (int cc = m.c1; cc <= m.c2; ++cc) {
+              const int sl = (cc == m.c1) ? m.c1_slot : 0;
+              M = fmaxf(M, __ldcg(ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * (kD + 2) + kD));
+            }
+            float L = 0.f;
+            for (int cc = m.c1; cc <= m.c2; ++cc) {
+              const int sl = (cc == m.c1) ? m.c1_slot : 0;
+              const float* r = ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * (kD + 2);
+              const float mc = __ldcg(r + kD);
+              L += (mc == -INFINITY) ? 0.f : exp2f(mc - M) * __ldcg(r + kD + 1);
+            }
+            s_comb[hh] = M;
+            s_comb[64 + hh] = L > 0.f ? 1.f / L : 0.f;
+          }
+          named_bar_sync(1, nthr);
+          for (int idx = threadIdx.x; idx < heads_cta * kD; idx += nthr) {
+            const int hh = idx / kD, d = idx % kD;
+            const float M = s_comb[hh], invL = s_comb[64 + hh];
+            float acc = 0.f;
+            for (int cc = m.c1; cc <= m.c2; ++cc) {
+              const int sl = (cc == m.c1) ? m.c1_slot : 0;
+              const float* r = ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * (kD + 2);
+              const float mc = __ldcg(r + kD);
+              if (mc != -INFINITY) acc = fmaf(exp2f(mc - M), __ldcg(r + d), acc);
+            }
+            out[(b * p.Hq + hg * heads_cta + hh) * kD + d] = from_f32<T>(acc * invL);
+          }
+          named_bar_sync(1, nthr);
+        }
+      }
+      m_used = -INFINITY;
+      l_part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      cur_seg = -1;
+    }
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&empty_bar[st]));
+    if (m.kind == 2) break;
+  }
+}
+
 struct Geometry {
   bool tma_path;
-  bool mma;  // tensor-core consumer (block size a multiple of 16)
+  bool mma;   // tensor-core consumer (block size a multiple of 16)
+  bool flat;  // persistent flat-partition kernel
+  int flat_grid;
+  size_t flat_smem;
   int HG, n_hg, G, split_blocks, max_splits, stages;
   uint32_t stage_bytes;
   size_t tiles_bytes;
@@ -760,6 +1131,16 @@ Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t 
   g.smem_bytes = tiles + fixed;
   if (g.smem_bytes > kSmemBudget) return g;
   g.tma_path = true;
+  // flags bit 1: keep the split kernel even where the persistent one applies
+  const int64_t nseg = (int64_t)g.n_hg * B;
+  g.flat = g.mma && nseg <= kFlatMaxSeg && !(cfg && (cfg->flags & 2));
+  if (g.flat) {
+    g.flat_grid = (cfg && cfg->tile_m > 0) ? cfg->tile_m : device_sm_count();
+    const size_t extra = (size_t)g.stages * (2 * 8 + sizeof(PageMeta)) + (size_t)(nseg + 1) * 8 +
+                         (size_t)B * 8 + 64 * 4 + 128 * 4 + 16;
+    g.flat_smem = (size_t)g.stages * g.stage_bytes + extra + 1024;
+    if (g.flat_smem > kSmemBudget) g.flat = false;
+  }
   return g;
 }
 
@@ -813,6 +1194,29 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
   int* tickets = static_cast<int*>(workspace);
   float* ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTicketBytes);
   float* ws_ml = ws_o + n_rows * kD;
+  if (geo.flat) {
+    FlatParams fp;
+    fp.B = B;
+    fp.Hq = Hq;
+    fp.Hkv = Hkv;
+    fp.num_blocks = num_blocks;
+    fp.block_size = bs;
+    fp.max_blocks = max_blocks;
+    fp.HG = geo.HG;
+    fp.n_hg = geo.n_hg;
+    fp.stages = geo.stages;
+    fp.nseg = (int)(geo.n_hg * B);
+    fp.stage_bytes = geo.stage_bytes;
+    fp.qscale = scale * 1.4426950408889634f;
+    auto fk = paged_decode_flat_kernel<T, IDX, G>;
+    cudaError_t e = cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)geo.flat_smem);
+    if (e != cudaSuccess) return launch_status(e);
+    fk<<<geo.flat_grid, (geo.HG + 1) * 32, geo.flat_smem, stream>>>(
+        tk, tv, static_cast<const T*>(q), static_cast<const IDX*>(block_table), static_cast<const IDX*>(ctx_len),
+        static_cast<T*>(out), reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTicketBytes),
+        static_cast<int*>(workspace), fp);
+    return launch_status(cudaGetLastError());
+  }
   auto kern = geo.mma ? paged_decode_kernel<T, IDX, G, true> : paged_decode_kernel<T, IDX, G, false>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)geo.smem_bytes);
@@ -826,6 +1230,7 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
 
 size_t workspace_bytes_for(int64_t B, int64_t Hq, int64_t D, const Geometry& geo) {
   if (!geo.tma_path) return 0;
+  if (geo.flat) return kTicketBytes + (size_t)geo.flat_grid * 2 * geo.HG * geo.G * (size_t)(D + 2) * 4;
   const size_t n_rows = (size_t)B * Hq * geo.max_splits;
   return kTicketBytes + n_rows * (size_t)(D + 2) * 4;
 }
@@ -846,7 +1251,12 @@ extern "C" size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq, int
   if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
   g.tma_path = true;
   g.max_splits = (int)((max_blocks + split - 1) / split);
-  return workspace_bytes_for(B, Hq, D, g);
+  const size_t split_need = workspace_bytes_for(B, Hq, D, g);
+  // persistent kernel: two partial slots per CTA of at most min(Hq, 64) heads
+  const int64_t grid = (cfg && cfg->tile_m > 0) ? cfg->tile_m : device_sm_count();
+  const int64_t heads = Hq < 64 ? Hq : 64;
+  const size_t flat_need = kTicketBytes + (size_t)grid * 2 * heads * (size_t)(D + 2) * 4;
+  return split_need > flat_need ? split_need : flat_need;
 }
 
 extern "C" int b200_paged_attention(const void* q, const void* k_cache, const void* v_cache,
@@ -870,7 +1280,7 @@ extern "C" int b200_paged_attention(const void* q, const void* k_cache, const vo
   const bool aligned = aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out);
   if (geo.tma_path && aligned && num_blocks * block_size < (1ll << 31)) {
     const size_t need = workspace_bytes_for(B, Hq, D, geo);
-    const bool single = geo.max_splits == 1;
+    const bool single = geo.max_splits == 1 && !geo.flat;
     if (!single && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
       return B200_ERR_WORKSPACE;
     return B200_DISPATCH_HALF(dtype, [&] {
