@@ -189,6 +189,43 @@ def secondary_ops(dev) -> dict:
     return res
 
 
+def sharded_gemm(dev, dist, ws) -> dict:
+    """quant_matmul split by output columns over the ranks: each rank runs the
+    tcgen05 GEMM on its W rows, then an NCCL all-gather over NVLink and one
+    placement copy assemble the full [M, N] output on every rank.  Timed on
+    the device as the max over ranks, all-gather included."""
+    from b200ops import workloads as WL
+    from b200ops.dist.collectives import sharded_int8_gemm
+    from b200ops.dist.sharding import column_shard
+    from b200ops.runtime import ops as K
+
+    M, N, Kd = 4096, 14336, 4096
+    A, W, sA, sW = WL.int8_gemm_inputs(M, N, Kd, device=dev)
+    rank = dist.get_rank()
+    n0, n1 = column_shard(N, ws, rank)
+    Wl, sWl = W[n0:n1].contiguous(), sW[n0:n1].contiguous()
+
+    def gemm(A_, W_, sA_, sW_, out):
+        K.int8_gemm(A_, W_, sA_, sW_, out=out)
+
+    fn = lambda: sharded_int8_gemm(A, Wl, sA, sWl, N, gemm)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    us = max_over_ranks(dist, e0.elapsed_time(e1) * 1e3 / reps, dev)
+    ops = 2 * M * N * Kd
+    return {f"int8_gemm_colsharded_M{M}_N{N}_K{Kd}_x{ws}": {"us": us, "TOPS_total": ops / us / 1e6,
+                                                           "includes": "local GEMM + NCCL all-gather + placement"}}
+
+
 # --------------------------------------------------------------------------- B200
 def run_b200(args, ws, rank, local, dist):
     from b200ops import workloads as WL
@@ -357,6 +394,44 @@ def run_reference(args, ws, rank):
     }
 
 
+PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-skinny", "flash", "rmsnorm")
+
+
+def profile_case(name: str, reps: int = 3) -> None:
+    """Runs one operator on a profiling-sized case `reps` times (for an ncu
+    capture of a single kernel: inputs larger than L2, a few GB at most)."""
+    from b200ops import workloads as WL
+    from b200ops.runtime import ops as K
+
+    dev = torch.device("cuda", 0)
+    if name in ("decode", "decode-split", "append"):
+        cache = WL.paged_cache(num_blocks=16384, block_size=BS, Hkv=HKV, D=D, device=dev)
+        if name == "append":
+            app = WL.decode_append_inputs(cache, n_tok=N_SEQ, Hq=HQ, device=dev)
+            fn = lambda: K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"],  # noqa: E731
+                                                app["sin"], app["slot_mapping"], cache.k_cache, cache.v_cache)
+        else:
+            att = WL.decode_attention_inputs(cache, B=N_SEQ, Hq=HQ, ctx_lo=512, ctx_hi=4096, device=dev)
+            cfg = {"flags": 2} if name == "decode-split" else None
+            fn = lambda: K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"],  # noqa: E731
+                                           att["context_len"], cfg=cfg)
+    elif name in ("gemm", "gemm-skinny"):
+        M = 16 if name == "gemm-skinny" else 4096
+        A, W, sA, sW = WL.int8_gemm_inputs(M, 14336, 4096, device=dev)
+        fn = lambda: K.int8_gemm(A, W, sA, sW)  # noqa: E731
+    elif name == "flash":
+        q, k, v = WL.flash_inputs(B=1, H=8, T=4096, device=dev)
+        fn = lambda: K.flash_attn(q, k, v, causal=True)  # noqa: E731
+    else:
+        x, w = WL.rmsnorm_inputs(device=dev)
+        fn = lambda: K.rmsnorm(x, w)  # noqa: E731
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+    assert K.read_device_error(dev) == 0
+    print(json.dumps({"case": name, "reps": reps, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -365,7 +440,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the per-op lines (GEMM, prefill, rmsnorm)")
+    ap.add_argument("--case", choices=PROFILE_CASES, default=None,
+                    help="run one operator on a small case for a profiler capture, then exit")
     args = ap.parse_args()
+    if args.case:
+        profile_case(args.case)
+        return
     ws, rank, local = dist_env()
     if args.impl == "reference":
         res = run_reference(args, ws, rank)
@@ -377,6 +457,8 @@ def main():
         res = run_b200(args, ws, rank, local, dist)
         if not args.no_secondary:
             sec = secondary_ops(torch.device("cuda", local))
+            if ws > 1:
+                sec.update(sharded_gemm(torch.device("cuda", local), dist, ws))
             if rank == 0:
                 res["secondary"] = sec
         if rank == 0:

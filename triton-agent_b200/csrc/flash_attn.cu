@@ -46,6 +46,7 @@ struct FlashParams {
   float sl2;        // scale * log2(e)
   int causal;
   int out_lse;
+  int poly_exp;     // half of the unmasked exponentials on the FMA pipe
 };
 
 template <int D>
@@ -77,6 +78,21 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe, to share the softmax's exponentials with the MUFU
+// unit: x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an integer,
+// exact for |x| < 2^22) and f in [-0.5, 0.5]; 2^f by the cubic
+// 1 + f(c1 + f(c2 + f c3)) fitted in this project by least squares on the
+// relative error (max 1.2e-4, well below the bf16 rounding P gets next);
+// 2^n is added to the exponent field.  Inputs are clamped to >= -126.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - 12582912.0f);
+  const float p = fmaf(fmaf(fmaf(0.0545928263f, f, 0.242218109f), f, 0.693368645f), f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 template <typename T>
@@ -250,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_kt; ++j) {
       const int s = j & 1;
-      if (!sm100::mbar_wait(sm100::smem_u32(&s_full[s]), (j >> 1) & 1)) {
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&s_full[s]), (j >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -303,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l = l * alpha + sum;
       // PV_{j-1} must be complete before P is overwritten or O is rescaled.
-      if (j > 0 && !sm100::mbar_wait(sm100::smem_u32(o_done), (j - 1) & 1)) {
+      if (j > 0 && !sm100::mbar_wait_warp(sm100::smem_u32(o_done), (j - 1) & 1)) {
         ok = false;
         break;
       }
@@ -337,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(p_full));
     }
     // epilogue
-    if (ok && n_kt > 0 && !sm100::mbar_wait(sm100::smem_u32(o_done), (n_kt - 1) & 1)) ok = false;
+    if (ok && n_kt > 0 && !sm100::mbar_wait_warp(sm100::smem_u32(o_done), (n_kt - 1) & 1)) ok = false;
     if (!ok) {
       b200_dev_error(kDevErrTimeoutMma);
       atomicExch(s_abort, 1);
@@ -350,6 +366,354 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c = 0; c < D; c += 32) {
       uint32_t o[32];
       sm100::tmem_ld_32x32b_x32(tO + lane_off + c, o);
+      sm100::tmem_wait_ld();
+      if (row_ok && ok) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c + 8 * v) = w;
+        }
+      }
+    }
+    if (p.out_lse && row_ok) lse[(int64_t)bh * p.T + qrow] = (m_used + log2f(l)) * 0.6931471805599453f;
+    sm100::tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Two-tile kernel: 256 query rows per CTA as tiles A and B that share every
+// K/V tile (half the shared-memory operand traffic per FLOP of the one-tile
+// kernel), with P kept in tensor memory.
+//
+// TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256, 256+D),
+// O_B [384, 384+D).  P_t is written as bf16 pairs into the first 64 columns
+// of S_t and read back as the A operand of O_t += P_t V (tcgen05.mma with A
+// from tensor memory), so no P tile lives in shared memory.
+// Warps: 0 TMA producer, 1 MMA issue + TMEM allocation, 2-3 idle, 4-7 softmax
+// of tile A, 8-11 softmax of tile B (warp w reads TMEM lanes 32*(w%4)..).
+// The MMA thread issues S_A(j), S_B(j), then alternates PV_A(j), S_A(j+1),
+// PV_B(j), S_B(j+1): while one softmax warpgroup turns S into P, the tensor
+// core works on the other tile.  tcgen05.mma ops of one thread complete in
+// issue order, so the completion of S_t(j) (the s_full barrier) also means
+// PV_t(j-1) is done -- O_t may be rescaled and P_t overwritten.
+// ---------------------------------------------------------------------------
+constexpr int kThreads2 = 384;
+
+template <int D>
+struct Flash2Smem {
+  static constexpr uint32_t kHalf = kBM * 128;         // one 64-dim box of 128 rows
+  static constexpr uint32_t kTile = (D / 64) * kHalf;  // Q, K or V tile
+  static constexpr uint32_t oQA = 0;
+  static constexpr uint32_t oQB = oQA + kTile;
+  static constexpr uint32_t oK0 = oQB + kTile;
+  static constexpr uint32_t oV0 = oK0 + kTile;
+  static constexpr uint32_t oK1 = oV0 + kTile;
+  static constexpr uint32_t oV1 = oK1 + kTile;
+  static constexpr uint32_t oBar = oV1 + kTile;
+  static constexpr uint32_t kTotal = oBar + 256 + 1024;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads2, 1)
+    flash_fwd2_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out, float* __restrict__ lse,
+                              FlashParams p) {
+  using L = Flash2Smem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = sm100::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int n_ct = (int)((p.T + 2 * kBM - 1) / (2 * kBM));
+  const int ct = n_ct - 1 - (int)blockIdx.y;  // heaviest first
+  const int64_t q0 = (int64_t)ct * 2 * kBM;
+  const int n_kt_all = (int)((p.S + kBN - 1) / kBN);
+  // key tiles each query tile needs (causal: up to its diagonal)
+  int n_kt[2];
+  for (int t = 0; t < 2; ++t) {
+    const int64_t last_row = q0 + (t + 1) * kBM - 1;
+    n_kt[t] = p.causal ? min(n_kt_all, (int)(last_row / kBN) + 1) : n_kt_all;
+  }
+  const int n_kt_max = n_kt[0] > n_kt[1] ? n_kt[0] : n_kt[1];
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [2 tiles]
+  uint64_t* p_full = bars + 9;    // [2 tiles]
+  uint64_t* o_done = bars + 11;   // [2 tiles]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(sm100::smem_u32(q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(sm100::smem_u32(&k_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&v_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&kv_empty[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&s_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&p_full[i]), 4);
+      sm100::mbar_init(sm100::smem_u32(&o_done[i]), 1);
+    }
+    *s_abort = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(sm100::smem_u32(tmem_slot), 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO[2] = {tmem + 256, tmem + 384};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_q);
+      sm100::tma_prefetch_desc(&tm_k);
+      sm100::tma_prefetch_desc(&tm_v);
+      const uint32_t qb = sm100::smem_u32(q_full);
+      sm100::mbar_arrive_expect_tx(qb, 2 * L::kTile);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + (t ? L::oQB : L::oQA) + h * L::kHalf, &tm_q, qb, h * 64,
+                             (int32_t)(q0 + t * kBM), bh);
+      int issued = 0;
+      for (int j = 0; j < n_kt_max; ++j) {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&kv_empty[s]), ((j >> 1) & 1) ^ 1)) {
+          b200_dev_error(kDevErrTimeoutEmpty);
+          atomicExch(s_abort, 1);
+          break;
+        }
+        if (*(volatile int*)s_abort) break;
+        const uint32_t kb = sm100::smem_u32(&k_full[s]);
+        const uint32_t vb = sm100::smem_u32(&v_full[s]);
+        sm100::mbar_arrive_expect_tx(kb, L::kTile);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + (s ? L::oK1 : L::oK0) + h * L::kHalf, &tm_k, kb, h * 64, j * kBN, bh);
+        sm100::mbar_arrive_expect_tx(vb, L::kTile);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + (s ? L::oV1 : L::oV0) + h * L::kHalf, &tm_v, vb, h * 64, j * kBN, bh);
+        ++issued;
+      }
+      if (!sm100::mbar_wait(sm100::smem_u32(q_full), 0)) b200_dev_error(kDevErrTimeoutFull);
+      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j) {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&k_full[s]), (j >> 1) & 1)) b200_dev_error(kDevErrTimeoutFull);
+        if (!sm100::mbar_wait(sm100::smem_u32(&v_full[s]), (j >> 1) & 1)) b200_dev_error(kDevErrTimeoutFull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_s = sm100::make_idesc(1, fmt, fmt, 0, 0, kBM, kBN);
+      constexpr uint32_t idesc_o = sm100::make_idesc(1, fmt, fmt, 0, 1, kBM, D);
+      bool ok = sm100::mbar_wait(sm100::smem_u32(q_full), 0);
+      auto issue_s = [&](int t, int j) -> bool {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&k_full[s]), (j >> 1) & 1)) return false;
+        sm100::tc_fence_after();
+        const uint32_t kbase = sbase + (s ? L::oK1 : L::oK0);
+        const uint32_t qbase = sbase + (t ? L::oQB : L::oQA);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kHalf + (kk & 3) * 32;
+          const uint64_t ad = sm100::make_smem_desc(qbase + off, 16, 1024, sm100::kSwizzle128B);
+          const uint64_t bd = sm100::make_smem_desc(kbase + off, 16, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ss(tS[t], ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        sm100::tc_commit(sm100::smem_u32(&s_full[t]));
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int s = j & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&p_full[t]), j & 1)) return false;
+        if (!sm100::mbar_wait(sm100::smem_u32(&v_full[s]), (j >> 1) & 1)) return false;
+        sm100::tc_fence_after();
+        const uint32_t vbase = sbase + (s ? L::oV1 : L::oV0);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // V: MN-major; 16 keys = two 8-row groups of 128 B (SBO 1024),
+          // head-dim halves one box (16 KB) apart (LBO).  P: 8 TMEM columns
+          // of bf16 pairs per 16 keys.
+          const uint64_t bd = sm100::make_smem_desc(vbase + kk * 2048, L::kHalf, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ts(tO[t], tS[t] + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        return true;
+      };
+      for (int t = 0; t < 2 && ok; ++t)
+        if (n_kt[t] > 0) ok = issue_s(t, 0);
+      for (int j = 0; ok && j < n_kt_max; ++j) {
+        if (*(volatile int*)s_abort) {
+          ok = false;
+          break;
+        }
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_kt[t]) continue;
+          ok = issue_pv(t, j);
+          if (ok && j + 1 < n_kt[t]) ok = issue_s(t, j + 1);
+          if (ok && j + 1 == n_kt[t]) sm100::tc_commit(sm100::smem_u32(&o_done[t]));
+        }
+        if (ok) sm100::tc_commit(sm100::smem_u32(&kv_empty[j & 1]));
+      }
+      if (!ok) {
+        b200_dev_error(kDevErrTimeoutFull);
+        atomicExch(s_abort, 1);
+        for (int t = 0; t < 2; ++t) sm100::tc_commit(sm100::smem_u32(&o_done[t]));
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- softmax
+    const int t = (warp >> 2) - 1;  // tile of this warpgroup
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int64_t qrow = q0 + t * kBM + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tSt = tS[t] + lane_off, tOt = tO[t] + lane_off;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    const int nj = n_kt[t];
+    for (int j = 0; j < nj; ++j) {
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&s_full[t]), j & 1)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const int64_t k0 = (int64_t)j * kBN;
+      int valid = kBN;
+      if ((k0 + kBN > p.S) || (p.causal && k0 + kBN - 1 > qrow)) {
+        const int64_t lim = (p.causal && qrow + 1 < p.S) ? qrow + 1 : p.S;
+        const int64_t nv = lim - k0;
+        valid = nv <= 0 ? 0 : (nv >= kBN ? kBN : (int)nv);
+      }
+      const bool full_tile = __all_sync(0xffffffffu, valid == kBN) != 0;
+      // pass 1: row max of the raw scores
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld_32x32b_x32(tSt + c * 32, v);
+        sm100::tmem_wait_ld();
+        if (full_tile) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(v[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = (c * 32 + i < valid) ? __uint_as_float(v[i]) : -INFINITY;
+            mx8[i & 7] = fmaxf(mx8[i & 7], x);
+          }
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.sl2;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m_used == -INFINITY) {
+        m_used = mx;
+      } else if (mx > m_used + kRescaleThreshold) {
+        alpha = ex2_approx(m_used - mx);
+        m_used = mx;
+        rescale = true;
+      }
+      // O_t holds PV_t(j-1), complete because S_t(j) is: rescale it if the max moved
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          sm100::tmem_ld_32x32b_x32(tOt + c, o);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          sm100::tmem_st_32x32b_x16(tOt + c, o);
+          sm100::tmem_st_32x32b_x16(tOt + c + 16, o + 16);
+        }
+      }
+      // pass 2: P = 2^(s * scale * log2 e - m) as bf16 pairs over the S columns
+      const float neg_m = -m_used;
+      float sum8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+      if (full_tile) {
+        // no masked key in this tile for any lane of the warp (the branch must
+        // be warp-uniform: both sides issue .sync.aligned tensor-memory loads
+        // and stores); optionally half of the exponentials on the FMA pipe
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t v[32];
+          sm100::tmem_ld_32x32b_x32(tSt + c * 32, v);
+          sm100::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(v[i]), p.sl2, neg_m));
+            const float x1 = fmaf(__uint_as_float(v[i + 1]), p.sl2, neg_m);
+            const float p1 = p.poly_exp ? ex2_poly(x1) : ex2_approx(x1);
+            sum8[(i >> 1) & 7] += p0 + p1;
+            pk[i >> 1] = pack2<T>(p0, p1);
+          }
+          sm100::tmem_st_32x32b_x16(tSt + c * 16, pk);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t v[32];
+          sm100::tmem_ld_32x32b_x32(tSt + c * 32, v);
+          sm100::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = (c * 32 + i < valid) ? ex2_approx(fmaf(__uint_as_float(v[i]), p.sl2, neg_m)) : 0.f;
+            const float p1 =
+                (c * 32 + i + 1 < valid) ? ex2_approx(fmaf(__uint_as_float(v[i + 1]), p.sl2, neg_m)) : 0.f;
+            sum8[(i >> 1) & 7] += p0 + p1;
+            pk[i >> 1] = pack2<T>(p0, p1);
+          }
+          sm100::tmem_st_32x32b_x16(tSt + c * 16, pk);
+        }
+      }
+      sm100::tmem_wait_st();
+      l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&p_full[t]));
+    }
+    // epilogue: O_t / l
+    if (ok && nj > 0 && !sm100::mbar_wait_warp(sm100::smem_u32(&o_done[t]), 0)) ok = false;
+    if (!ok) {
+      b200_dev_error(kDevErrTimeoutMma);
+      atomicExch(s_abort, 1);
+    }
+    sm100::tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const bool row_ok = qrow < p.T;
+    T* orow = out + ((int64_t)bh * p.T + qrow) * D;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t o[32];
+      sm100::tmem_ld_32x32b_x32(tOt + c, o);
       sm100::tmem_wait_ld();
       if (row_ok && ok) {
 #pragma unroll
@@ -427,7 +791,7 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const T* __restrict_
 
 template <typename T, int D>
 int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, const FlashParams& p,
-              cudaStream_t s) {
+              bool two_tile, cudaStream_t s) {
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tq, tk, tv;
@@ -446,6 +810,15 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, 
     st = encode_tensor_map(&tv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
+  if (two_tile) {
+    auto kern = flash_fwd2_tcgen05_kernel<T, D>;
+    const int smem = (int)Flash2Smem<D>::kTotal;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return launch_status(e);
+    dim3 grid((unsigned)(p.B * p.H), (unsigned)((p.T + 2 * kBM - 1) / (2 * kBM)));
+    kern<<<grid, kThreads2, smem, s>>>(tq, tk, tv, static_cast<T*>(o), lse, p);
+    return launch_status(cudaGetLastError());
+  }
   auto kern = flash_fwd_tcgen05_kernel<T, D>;
   const int smem = (int)FlashSmem<D>::kTotal;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -463,7 +836,6 @@ using namespace b200;
 extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
                                int64_t H, int64_t T, int64_t S, int64_t D, float scale, int32_t causal,
                                int32_t dtype, const b200_launch_cfg* cfg, void* stream) {
-  (void)cfg;
   if (int e = injected_error("flash_attn")) return e;
   if (B < 0 || H < 0 || T < 0 || S < 0 || D <= 0) return B200_ERR_BAD_ARG;
   if (causal && T != S) return B200_ERR_BAD_ARG;  // the reference's tril mask assumes T == S
@@ -480,13 +852,16 @@ extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void
   p.sl2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.out_lse = lse != nullptr;
+  p.poly_exp = (cfg && (cfg->flags & 2)) ? 1 : 0;  // flags bit 1
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc = (D == 64 || D == 128) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) &&
                   B * H <= 0x7fffffffLL && p.n_qt <= 65535 && T < (1ll << 31) && S < (1ll << 31);
   if (tc) {
     return B200_DISPATCH_HALF(dtype, [&] {
-      return D == 128 ? launch_tc<scalar_t, 128>(q, k, v, o, lse, p, s)
-                      : launch_tc<scalar_t, 64>(q, k, v, o, lse, p, s);
+      // flags bit 0: the one-tile kernel (P staged in shared memory)
+      const bool two_tile = !(cfg && (cfg->flags & 1));
+      return D == 128 ? launch_tc<scalar_t, 128>(q, k, v, o, lse, p, two_tile, s)
+                      : launch_tc<scalar_t, 64>(q, k, v, o, lse, p, two_tile, s);
     });
   }
   if (D > 256) return B200_ERR_UNSUPPORTED;

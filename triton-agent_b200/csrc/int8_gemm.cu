@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int lt = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++lt) {
       const int a = lt & 1;
-      if (!sm100::mbar_wait(sm100::smem_u32(&bars.acc_full[a]), (lt >> 1) & 1)) {
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_full[a]), (lt >> 1) & 1)) {
         set_abort(bars, kDevErrTimeoutMma);
         break;
       }
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int quarter = warp & 3;
     const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
-    const bool ok = sm100::mbar_wait(sm100::smem_u32(&bars.acc_full[0]), 0);
+    const bool ok = sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_full[0]), 0);
     if (!ok) set_abort(bars, kDevErrTimeoutMma);
     sm100::tc_fence_after();
     uint32_t acc[MN];

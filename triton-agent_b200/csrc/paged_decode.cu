@@ -260,7 +260,7 @@ __device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, u
 
   for (int i = 0; i < npages; ++i) {
     const int s = i % p.stages;
-    if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+    if (!sm100::mbar_wait_warp(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
       b200_dev_error(kDevErrTimeoutFull);
       atomicExch(&s_misc[1], 1);
       break;
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(288, 1)
 
     for (int i = 0; i < npages; ++i) {
       const int s = i % p.stages;
-      if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&full_bar[s]), (i / p.stages) & 1)) {
         b200_dev_error(kDevErrTimeoutFull);
         atomicExch(&s_misc[1], 1);
         break;
@@ -976,7 +976,7 @@ __global__ void __launch_bounds__(288, 1)
   const int nthr = HG * 32;
   for (int it = 0;; ++it) {
     const int st = it % p.stages;
-    if (!sm100::mbar_wait(sm100::smem_u32(&full_bar[st]), (it / p.stages) & 1)) {
+    if (!sm100::mbar_wait_warp(sm100::smem_u32(&full_bar[st]), (it / p.stages) & 1)) {
       b200_dev_error(kDevErrTimeoutFull);
       atomicExch(&s_flags[0], 1);
       break;

@@ -80,6 +80,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// Warp-uniform variant for warps that go on to issue .sync.aligned
+// instructions (tcgen05.ld/st, ldmatrix, mma.sync, bar.sync): every lane
+// waits, and the warp proceeds (or gives up) as one.  Call with all 32 lanes.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity,
+                                               uint64_t timeout_ns = kWaitTimeoutNs) {
+  const bool ok = mbar_wait(bar, parity, timeout_ns);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
