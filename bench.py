@@ -49,13 +49,15 @@ def dist_env():
     return ws, rank, local
 
 
-def init_dist(ws):
+def init_dist(ws, local):
     if ws > 1:
         import datetime
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         return dist
     return None
 
@@ -429,7 +431,10 @@ def profile_case(name: str, reps: int = 3) -> None:
         fn()
     torch.cuda.synchronize()
     assert K.read_device_error(dev) == 0
-    print(json.dumps({"case": name, "reps": reps, "ok": True}))
+    info = {"case": name, "reps": reps, "ok": True}
+    if name in ("decode", "decode-split"):
+        info["algorithmic_bytes"] = WL.decode_bytes(att["context_len"], HQ, HKV, D, BS)
+    print(json.dumps(info))
 
 
 def main():
@@ -452,7 +457,7 @@ def main():
         if res is not None:
             print(json.dumps(res))
         return
-    dist = init_dist(ws)
+    dist = init_dist(ws, local)
     try:
         res = run_b200(args, ws, rank, local, dist)
         if not args.no_secondary:

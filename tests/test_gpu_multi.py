@@ -1,0 +1,83 @@
+"""Multi-GPU paths (one process per GPU, NCCL over NVLink): the
+column-sharded INT8 GEMM with its all-gather equals the single-GPU GEMM bit
+for bit, and batch-sharded decode (each rank owns its sequences' KV pages)
+equals the single-GPU decode of the same sequences.  Skipped on a box with
+one GPU."""
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    sys.path[:0] = [str(REPO), str(REPO / "triton-agent_b200")]
+    import datetime
+
+    import torch.distributed as dist
+
+    from b200ops import workloads as WL
+    from b200ops.dist.collectives import sharded_int8_gemm
+    from b200ops.dist.sharding import column_shard, shard_sequences
+    from b200ops.runtime import ops as K
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        # column-sharded GEMM
+        M, N, Kd = 512, 3000, 1024
+        A, W, sA, sW = WL.int8_gemm_inputs(M, N, Kd, device=dev, seed=5)
+        full = K.int8_gemm(A, W, sA, sW)
+        n0, n1 = column_shard(N, world, rank)
+        C = sharded_int8_gemm(A, W[n0:n1].contiguous(), sA, sW[n0:n1].contiguous(), N,
+                              lambda a, w, s1, s2, out: K.int8_gemm(a, w, s1, s2, out=out))
+        gemm_ok = bool(torch.equal(C, full))
+        # batch-sharded decode: same inputs on every rank, each computes its share
+        cache = WL.paged_cache(num_blocks=2048, block_size=16, Hkv=8, D=128, device=dev, seed=6)
+        att = WL.decode_attention_inputs(cache, B=16, Hq=32, ctx_lo=100, ctx_hi=1500, device=dev, seed=6)
+        ref = K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"])
+        parts = shard_sequences(att["context_len"].cpu().tolist(), world)
+        mine = torch.tensor(parts[rank], dtype=torch.long, device=dev)
+        out = K.paged_attention(att["q"][mine].contiguous(), cache.k_cache, cache.v_cache,
+                                att["block_table"][mine].contiguous(), att["context_len"][mine].contiguous())
+        dec_ok = bool(torch.allclose(out.float(), ref[mine].float(), atol=2e-2, rtol=0))
+        torch.cuda.synchronize()
+        q.put((rank, gemm_ok, dec_ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_gemm_and_decode_match_single_gpu():
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    world = min(world, 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    assert all(g for _, g, _ in res), res
+    assert all(d for _, _, d in res), res

@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN; c += 32) {
         uint32_t acc[32];
         sm100::tmem_ld_32x32b_x32(t_row + c, acc);
-        sm100::tmem_wait_ld();
+        sm100::tmem_wait_ld_regs(acc);
         if (row < p.M && !aborted(bars))
           epilogue_chunk<OutT>(acc, row, (int64_t)n_tile * BN + c, sA, sW, C, acc_out, p);
       }
@@ -352,7 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int c = 0; c < MN; c += 16)
       sm100::tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + c, acc + c);
-    sm100::tmem_wait_ld();
+#pragma unroll
+    for (int c = 0; c < MN; c += 16) sm100::tmem_wait_ld_regs16(acc + c);
     if (nk == 0) {
 #pragma unroll
       for (int j = 0; j < MN; ++j) acc[j] = 0;
