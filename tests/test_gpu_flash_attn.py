@@ -13,13 +13,13 @@ pytestmark = pytest.mark.gpu
 ATOL = 2e-2
 
 
-def check(B, H, T, S, D, causal, dtype, cuda_device, rows=None, seed=0):
+def check(B, H, T, S, D, causal, dtype, cuda_device, rows=None, seed=0, cfg=None):
     g = torch.Generator(device=cuda_device).manual_seed(seed)
     q = torch.randn(B, H, T, D, generator=g, device=cuda_device).to(dtype)
     k = torch.randn(B, H, S, D, generator=g, device=cuda_device).to(dtype)
     v = torch.randn(B, H, S, D, generator=g, device=cuda_device).to(dtype)
     lse = torch.empty(B, H, T, device=cuda_device, dtype=torch.float32)
-    out = K.flash_attn(q, k, v, causal=causal, lse=lse)
+    out = K.flash_attn(q, k, v, causal=causal, lse=lse, cfg=cfg)
     torch.cuda.synchronize()
     assert K.read_device_error() == 0
     exp = O.flash_attn(q.cpu(), k.cpu(), v.cpu(), causal, rows=rows)
@@ -30,6 +30,14 @@ def check(B, H, T, S, D, causal, dtype, cuda_device, rows=None, seed=0):
         exp = exp.reshape(B * H, T, D)
     torch.testing.assert_close(got.cpu().float(), exp, rtol=0, atol=ATOL)
     return out
+
+
+# launch flags: 0 three-warpgroup kernel (default), 2 the same with part of
+# the exponentials on the FMA pipe, 4 two-tile kernel, 1 one-tile kernel
+@pytest.mark.parametrize("flags", [0, 2, 4, 1])
+@pytest.mark.parametrize("causal,T,S,D", [(True, 1000, 1000, 128), (False, 130, 517, 128), (True, 700, 700, 64)])
+def test_kernel_variants(flags, causal, T, S, D, cuda_device):
+    check(1, 3, T, S, D, causal, torch.bfloat16, cuda_device, cfg={"flags": flags})
 
 
 def test_golden_reference_cases(golden_dir, cuda_device):

@@ -738,6 +738,350 @@ __global__ void __launch_bounds__(kThreads2, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Three-warpgroup kernel (default): the two-tile work split and TMEM layout,
+// plus
+//  * K and V tiles in one ring of kRing3 single-tile slots, loaded in the
+//    order K0 V0 K1 V1 ...; each slot is handed back by a tcgen05.commit as
+//    soon as the last MMA reading it completes (K_j after S_B(j), V_j after
+//    PV_B(j)), so key tile j+2 is already streaming while tile j is in use;
+//  * register reallocation: the TMA/MMA warpgroup drops to 56 registers and
+//    the two softmax warpgroups rise to 224, so a thread keeps its whole
+//    128-column score row in registers and reads tensor memory once per tile;
+//  * three-input max and packed fp32x2 FMA/add in the softmax.
+// Warpgroup 0: warp 0 TMA producer, warp 1 MMA issue + TMEM allocation,
+// warps 2-3 idle; warpgroups 1 and 2: softmax of tiles A and B.
+// ---------------------------------------------------------------------------
+constexpr int kThreads3 = 384;
+constexpr int kRing3 = 5;
+constexpr int kRegsLow3 = 56, kRegsHigh3 = 224;
+// launch registers per thread the reallocation needs (128 * low + 256 * high <= 384 * launch)
+constexpr int kRegsLaunch3 = (128 * kRegsLow3 + 256 * kRegsHigh3 + kThreads3 - 1) / kThreads3;
+
+template <int D>
+struct Flash3Smem {
+  static constexpr uint32_t kHalf = kBM * 128;         // one 64-dim box of 128 rows
+  static constexpr uint32_t kTile = (D / 64) * kHalf;  // Q, K or V tile
+  static constexpr uint32_t oQA = 0;
+  static constexpr uint32_t oQB = kTile;
+  static constexpr uint32_t oRing = 2 * kTile;
+  static constexpr uint32_t oBar = oRing + kRing3 * kTile;
+  static constexpr uint32_t kTotal = oBar + 256 + 1024;
+};
+
+// P = 2^(s * sl2 - m) over one 128-column score row held in registers,
+// written as bf16/fp16 pairs to tensor memory (columns [0, 64) of the S
+// tile); returns the row sum of the (unrounded) probabilities.  kPoly of
+// every 8 pairs take the FMA-pipe exponential (only on unmasked tiles).
+template <typename T, int kPoly>
+__device__ __forceinline__ float softmax_row_to_tmem(const uint32_t (&v)[kBN], float sl2, float neg_m,
+                                                     uint32_t taddr) {
+  float s[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s[i] = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int c = h * 64 + 2 * i;
+      float x0, x1;
+      sm100::ffma2_bcast(x0, x1, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), sl2, neg_m);
+      float p0, p1;
+      if ((i & 7) < kPoly) {
+        p0 = ex2_poly(x0);
+        p1 = ex2_poly(x1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      sm100::fadd2_acc(s[2 * (i & 3)], s[2 * (i & 3) + 1], p0, p1);
+      pk[i] = pack2<T>(p0, p1);
+    }
+    sm100::tmem_st_32x32b_x32(taddr + h * 32, pk);
+  }
+  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads3, 1)
+    flash_fwd3_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out, float* __restrict__ lse,
+                              FlashParams p) {
+  using L = Flash3Smem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = sm100::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int n_ct = (int)((p.T + 2 * kBM - 1) / (2 * kBM));
+  const int ct = n_ct - 1 - (int)blockIdx.y;  // heaviest first
+  const int64_t q0 = (int64_t)ct * 2 * kBM;
+  const int n_kt_all = (int)((p.S + kBN - 1) / kBN);
+  // key tiles each query tile needs (causal: up to its diagonal); n_kt1 >= n_kt0
+  // (scalars, not an array indexed by the tile: that would live in local memory)
+  const int n_kt0 = p.causal ? min(n_kt_all, (int)((q0 + kBM - 1) / kBN) + 1) : n_kt_all;
+  const int n_kt1 = p.causal ? min(n_kt_all, (int)((q0 + 2 * kBM - 1) / kBN) + 1) : n_kt_all;
+  const int n_kt_max = n_kt1;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* ring_full = bars + 1;               // [kRing3]
+  uint64_t* ring_empty = bars + 1 + kRing3;     // [kRing3]
+  uint64_t* s_full = bars + 1 + 2 * kRing3;     // [2 tiles]
+  uint64_t* p_full = s_full + 2;                // [2 tiles]
+  uint64_t* o_done = s_full + 4;                // [2 tiles]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 6);
+  int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(sm100::smem_u32(q_full), 1);
+    for (int i = 0; i < kRing3; ++i) {
+      sm100::mbar_init(sm100::smem_u32(&ring_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&ring_empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(sm100::smem_u32(&s_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&p_full[i]), 4);
+      sm100::mbar_init(sm100::smem_u32(&o_done[i]), 1);
+    }
+    *s_abort = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(sm100::smem_u32(tmem_slot), 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S_t at 128 t, O_t at 256 + 128 t
+
+  if (warp < 4) {
+    sm100::setmaxnreg_dec<kRegsLow3>();
+    if (warp == 0 && lane == 0) {
+      // ------------------------------------------------------------ producer
+      sm100::tma_prefetch_desc(&tm_q);
+      sm100::tma_prefetch_desc(&tm_k);
+      sm100::tma_prefetch_desc(&tm_v);
+      const uint32_t qb = sm100::smem_u32(q_full);
+      sm100::mbar_arrive_expect_tx(qb, 2 * L::kTile);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + (t ? L::oQB : L::oQA) + h * L::kHalf, &tm_q, qb, h * 64,
+                             (int32_t)(q0 + t * kBM), bh);
+      const int n_items = 2 * n_kt_max;
+      int issued = 0;
+      for (int it = 0; it < n_items; ++it) {
+        const int slot = it % kRing3;
+        if (!sm100::mbar_wait(sm100::smem_u32(&ring_empty[slot]), ((it / kRing3) & 1) ^ 1)) {
+          b200_dev_error(kDevErrTimeoutEmpty);
+          atomicExch(s_abort, 1);
+          break;
+        }
+        if (*(volatile int*)s_abort) break;
+        const uint32_t fb = sm100::smem_u32(&ring_full[slot]);
+        const CUtensorMap* map = (it & 1) ? &tm_v : &tm_k;
+        sm100::mbar_arrive_expect_tx(fb, L::kTile);
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h)
+          sm100::tma_load_3d(sbase + L::oRing + slot * L::kTile + h * L::kHalf, map, fb, h * 64,
+                             (it >> 1) * kBN, bh);
+        ++issued;
+      }
+      // no copy may still be writing shared memory when the CTA exits
+      if (!sm100::mbar_wait(sm100::smem_u32(q_full), 0)) b200_dev_error(kDevErrTimeoutFull);
+      for (int it = issued - 1; it >= 0 && it >= issued - kRing3; --it)
+        if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[it % kRing3]), (it / kRing3) & 1))
+          b200_dev_error(kDevErrTimeoutFull);
+    } else if (warp == 1 && lane == 0) {
+      // ----------------------------------------------------------- MMA issue
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_s = sm100::make_idesc(1, fmt, fmt, 0, 0, kBM, kBN);
+      constexpr uint32_t idesc_o = sm100::make_idesc(1, fmt, fmt, 0, 1, kBM, D);
+      bool ok = sm100::mbar_wait(sm100::smem_u32(q_full), 0);
+      auto ring_wait = [&](int it) -> uint32_t {
+        const int slot = it % kRing3;
+        if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[slot]), (it / kRing3) & 1)) return 0u;
+        sm100::tc_fence_after();
+        return sbase + L::oRing + slot * L::kTile;
+      };
+      auto release = [&](int it) { sm100::tc_commit(sm100::smem_u32(&ring_empty[it % kRing3])); };
+      auto issue_s = [&](int t, int j) -> bool {
+        const uint32_t kbase = ring_wait(2 * j);
+        if (!kbase) return false;
+        const uint32_t qbase = sbase + (t ? L::oQB : L::oQA);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kHalf + (kk & 3) * 32;
+          const uint64_t ad = sm100::make_smem_desc(qbase + off, 16, 1024, sm100::kSwizzle128B);
+          const uint64_t bd = sm100::make_smem_desc(kbase + off, 16, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ss(tmem + t * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        sm100::tc_commit(sm100::smem_u32(&s_full[t]));
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!sm100::mbar_wait(sm100::smem_u32(&p_full[t]), j & 1)) return false;
+        const uint32_t vbase = ring_wait(2 * j + 1);
+        if (!vbase) return false;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // V: MN-major; 16 keys = two 8-row groups of 128 B (SBO 1024),
+          // head-dim halves one box (16 KB) apart (LBO).  P: 8 TMEM columns
+          // of bf16 pairs per 16 keys.
+          const uint64_t bd = sm100::make_smem_desc(vbase + kk * 2048, L::kHalf, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        return true;
+      };
+      for (int t = 0; t < 2 && ok; ++t) ok = issue_s(t, 0);
+      if (ok) release(0);  // K_0
+      for (int j = 0; ok && j < n_kt_max; ++j) {
+        if (*(volatile int*)s_abort) {
+          ok = false;
+          break;
+        }
+        for (int t = 0; t < 2 && ok; ++t) {
+          const int nkt = t ? n_kt1 : n_kt0;
+          if (j >= nkt) continue;
+          ok = issue_pv(t, j);
+          if (ok && t == 1) release(2 * j + 1);  // V_j: tile B reads it last
+          if (ok && j + 1 < nkt) ok = issue_s(t, j + 1);
+          if (ok && j + 1 == nkt) sm100::tc_commit(sm100::smem_u32(&o_done[t]));
+        }
+        if (ok && j + 1 < n_kt_max) release(2 * j + 2);  // K_{j+1}
+      }
+      if (!ok) {
+        b200_dev_error(kDevErrTimeoutFull);
+        atomicExch(s_abort, 1);
+        for (int t = 0; t < 2; ++t) sm100::tc_commit(sm100::smem_u32(&o_done[t]));
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    sm100::setmaxnreg_inc<kRegsHigh3>();
+    const int t = (warp >> 2) - 1;  // tile of this warpgroup
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int64_t qrow = q0 + t * kBM + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tSt = tmem + t * 128 + lane_off, tOt = tmem + 256 + t * 128 + lane_off;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    const int nj = t ? n_kt1 : n_kt0;
+    for (int j = 0; j < nj; ++j) {
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&s_full[t]), j & 1)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      uint32_t v[kBN];
+      sm100::tmem_ld_32x32b_x64(tSt, v);
+      sm100::tmem_ld_32x32b_x64(tSt + 64, v + 64);
+      sm100::tmem_wait_ld();
+      const int64_t k0 = (int64_t)j * kBN;
+      int valid = kBN;
+      if ((k0 + kBN > p.S) || (p.causal && k0 + kBN - 1 > qrow)) {
+        const int64_t lim = (p.causal && qrow + 1 < p.S) ? qrow + 1 : p.S;
+        const int64_t nv = lim - k0;
+        valid = nv <= 0 ? 0 : (nv >= kBN ? kBN : (int)nv);
+      }
+      const bool full_tile = __all_sync(0xffffffffu, valid == kBN) != 0;
+      if (!full_tile) {
+#pragma unroll
+        for (int i = 0; i < kBN; ++i)
+          if (i >= valid) v[i] = 0xff800000u;  // -inf: max ignores it, 2^-inf = 0
+      }
+      float mx4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kBN; i += 8) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          mx4[a] = sm100::fmax3(mx4[a], __uint_as_float(v[i + 2 * a]), __uint_as_float(v[i + 2 * a + 1]));
+      }
+      const float mx = sm100::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * p.sl2;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m_used == -INFINITY) {
+        m_used = mx;
+      } else if (mx > m_used + kRescaleThreshold) {
+        alpha = ex2_approx(m_used - mx);
+        m_used = mx;
+        rescale = true;
+      }
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      float rs;
+      if (full_tile && p.poly_exp)
+        rs = softmax_row_to_tmem<T, 2>(v, p.sl2, neg_m, tSt);
+      else
+        rs = softmax_row_to_tmem<T, 0>(v, p.sl2, neg_m, tSt);
+      // O_t holds PV_t(j-1), complete because S_t(j) is: rescale it if the
+      // max moved (before P_t(j) is released to the MMA)
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          sm100::tmem_ld_32x32b_x32(tOt + c, o);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float y0, y1;
+            sm100::fmul2_bcast(y0, y1, __uint_as_float(o[i]), __uint_as_float(o[i + 1]), alpha);
+            o[i] = __float_as_uint(y0);
+            o[i + 1] = __float_as_uint(y1);
+          }
+          sm100::tmem_st_32x32b_x32(tOt + c, o);
+        }
+      }
+      sm100::tmem_wait_st();
+      l = l * alpha + rs;
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&p_full[t]));
+    }
+    // epilogue: O_t / l
+    if (ok && nj > 0 && !sm100::mbar_wait_warp(sm100::smem_u32(&o_done[t]), 0)) ok = false;
+    if (!ok) {
+      b200_dev_error(kDevErrTimeoutMma);
+      atomicExch(s_abort, 1);
+    }
+    sm100::tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const bool row_ok = qrow < p.T;
+    T* orow = out + ((int64_t)bh * p.T + qrow) * D;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t o[32];
+      sm100::tmem_ld_32x32b_x32(tOt + c, o);
+      sm100::tmem_wait_ld();
+      if (row_ok && ok) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c + 8 * v) = w;
+        }
+      }
+    }
+    if (p.out_lse && row_ok) lse[(int64_t)bh * p.T + qrow] = (m_used + log2f(l)) * 0.6931471805599453f;
+    sm100::tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // General fallback for head dims the tensor-core path does not cover (<= 256):
 // one warp per query row, lanes over keys, fp32 online softmax.
 // ---------------------------------------------------------------------------
@@ -791,7 +1135,7 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const T* __restrict_
 
 template <typename T, int D>
 int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, const FlashParams& p,
-              bool two_tile, cudaStream_t s) {
+              int variant, cudaStream_t s) {
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tq, tk, tv;
@@ -810,7 +1154,25 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, 
     st = encode_tensor_map(&tv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
-  if (two_tile) {
+  if (variant == 3) {
+    auto kern = flash_fwd3_tcgen05_kernel<T, D>;
+    const int smem = (int)Flash3Smem<D>::kTotal;
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return launch_status(e);
+    // the softmax warpgroups' setmaxnreg.inc draws on the launch registers
+    if (fa.numRegs < kRegsLaunch3) variant = 2;
+  }
+  if (variant == 3) {
+    auto kern = flash_fwd3_tcgen05_kernel<T, D>;
+    const int smem = (int)Flash3Smem<D>::kTotal;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return launch_status(e);
+    dim3 grid((unsigned)(p.B * p.H), (unsigned)((p.T + 2 * kBM - 1) / (2 * kBM)));
+    kern<<<grid, kThreads3, smem, s>>>(tq, tk, tv, static_cast<T*>(o), lse, p);
+    return launch_status(cudaGetLastError());
+  }
+  if (variant == 2) {
     auto kern = flash_fwd2_tcgen05_kernel<T, D>;
     const int smem = (int)Flash2Smem<D>::kTotal;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -858,10 +1220,12 @@ extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void
                   B * H <= 0x7fffffffLL && p.n_qt <= 65535 && T < (1ll << 31) && S < (1ll << 31);
   if (tc) {
     return B200_DISPATCH_HALF(dtype, [&] {
-      // flags bit 0: the one-tile kernel (P staged in shared memory)
-      const bool two_tile = !(cfg && (cfg->flags & 1));
-      return D == 128 ? launch_tc<scalar_t, 128>(q, k, v, o, lse, p, two_tile, s)
-                      : launch_tc<scalar_t, 64>(q, k, v, o, lse, p, two_tile, s);
+      // flags bit 0: the one-tile kernel (P staged in shared memory);
+      // bit 2: the two-tile kernel without register reallocation
+      const int fl = cfg ? cfg->flags : 0;
+      const int variant = (fl & 1) ? 1 : (fl & 4) ? 2 : 3;
+      return D == 128 ? launch_tc<scalar_t, 128>(q, k, v, o, lse, p, variant, s)
+                      : launch_tc<scalar_t, 64>(q, k, v, o, lse, p, variant, s);
     });
   }
   if (D > 256) return B200_ERR_UNSUPPORTED;
