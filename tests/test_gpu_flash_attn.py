@@ -32,12 +32,14 @@ def check(B, H, T, S, D, causal, dtype, cuda_device, rows=None, seed=0, cfg=None
     return out
 
 
-# launch flags: 0 three-warpgroup kernel (default), 2 the same with part of
-# the exponentials on the FMA pipe, 4 two-tile kernel, 1 one-tile kernel
-@pytest.mark.parametrize("flags", [0, 2, 4, 1])
+# launch flags: 0 three-warpgroup kernel (default); 8 the same releasing P
+# to the MMA as one tile; 4 two-tile kernel (+2: half its exponentials on
+# the FMA pipe); 1 one-tile kernel.  split: heads per CTA scheduling group.
+@pytest.mark.parametrize("cfg", [{"flags": 0}, {"flags": 8}, {"flags": 0, "split": 1}, {"flags": 0, "split": 5},
+                                 {"flags": 4}, {"flags": 6}, {"flags": 1}])
 @pytest.mark.parametrize("causal,T,S,D", [(True, 1000, 1000, 128), (False, 130, 517, 128), (True, 700, 700, 64)])
-def test_kernel_variants(flags, causal, T, S, D, cuda_device):
-    check(1, 3, T, S, D, causal, torch.bfloat16, cuda_device, cfg={"flags": flags})
+def test_kernel_variants(cfg, causal, T, S, D, cuda_device):
+    check(2, 3, T, S, D, causal, torch.bfloat16, cuda_device, cfg=cfg)
 
 
 def test_golden_reference_cases(golden_dir, cuda_device):

@@ -46,7 +46,8 @@ struct FlashParams {
   float sl2;        // scale * log2(e)
   int causal;
   int out_lse;
-  int poly_exp;     // half of the unmasked exponentials on the FMA pipe
+  int poly_exp;     // unmasked exponentials partly on the FMA pipe
+  int head_group;   // heads per CTA scheduling group (three-warpgroup kernel)
 };
 
 template <int D>
@@ -812,9 +813,18 @@ __global__ void __launch_bounds__(kThreads3, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = sm100::smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // CTA order: heads in groups of p.head_group; within a group, the
+  // heaviest query tiles (causal) of all its heads first.  CTAs running
+  // together then share a few heads' K/V through L2, and long tiles start
+  // before short ones.
   const int n_ct = (int)((p.T + 2 * kBM - 1) / (2 * kBM));
-  const int ct = n_ct - 1 - (int)blockIdx.y;  // heaviest first
+  const int64_t BH = p.B * p.H;
+  const int64_t lin = blockIdx.x;
+  const int64_t grp = lin / ((int64_t)p.head_group * n_ct);
+  const int64_t rem = lin - grp * p.head_group * n_ct;
+  const int64_t gh = min((int64_t)p.head_group, BH - grp * p.head_group);  // heads in this group
+  const int bh = (int)(grp * p.head_group + rem % gh);
+  const int ct = n_ct - 1 - (int)(rem / gh);
   const int64_t q0 = (int64_t)ct * 2 * kBM;
   const int n_kt_all = (int)((p.S + kBN - 1) / kBN);
   // key tiles each query tile needs (causal: up to its diagonal); n_kt1 >= n_kt0
@@ -1168,8 +1178,9 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, 
     const int smem = (int)Flash3Smem<D>::kTotal;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return launch_status(e);
-    dim3 grid((unsigned)(p.B * p.H), (unsigned)((p.T + 2 * kBM - 1) / (2 * kBM)));
-    kern<<<grid, kThreads3, smem, s>>>(tq, tk, tv, static_cast<T*>(o), lse, p);
+    const int64_t n_cta = p.B * p.H * ((p.T + 2 * kBM - 1) / (2 * kBM));
+    if (n_cta > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
+    kern<<<(unsigned)n_cta, kThreads3, smem, s>>>(tq, tk, tv, static_cast<T*>(o), lse, p);
     return launch_status(cudaGetLastError());
   }
   if (variant == 2) {
@@ -1215,6 +1226,7 @@ extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void
   p.causal = causal ? 1 : 0;
   p.out_lse = lse != nullptr;
   p.poly_exp = (cfg && (cfg->flags & 2)) ? 1 : 0;  // flags bit 1
+  p.head_group = (cfg && cfg->split > 0) ? cfg->split : 8;  // split: heads per scheduling group
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc = (D == 64 || D == 128) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) &&
                   B * H <= 0x7fffffffLL && p.n_qt <= 65535 && T < (1ll << 31) && S < (1ll << 31);

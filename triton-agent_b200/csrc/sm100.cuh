@@ -305,6 +305,19 @@ __device__ __forceinline__ void ffma2_bcast(float& y0, float& y1, float a0, floa
       : "f"(a0), "f"(a1), "f"(b), "f"(c));
 }
 
+// (a0, a1) * (b0, b1) + (c0, c1) as one fp32x2 instruction.
+__device__ __forceinline__ void ffma2(float& y0, float& y1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(y0), "=f"(y1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
 // (s0, s1) += (a0, a1) as one fp32x2 instruction.
 __device__ __forceinline__ void fadd2_acc(float& s0, float& s1, float a0, float a1) {
   asm("{\n\t.reg .b64 rs, ra;\n\t"
