@@ -32,11 +32,12 @@ def check(B, H, T, S, D, causal, dtype, cuda_device, rows=None, seed=0, cfg=None
     return out
 
 
-# launch flags: 0 three-warpgroup kernel (default); 8 the same releasing P
-# to the MMA as one tile; 4 two-tile kernel (+2: half its exponentials on
-# the FMA pipe); 1 one-tile kernel.  split: heads per CTA scheduling group.
-@pytest.mark.parametrize("cfg", [{"flags": 0}, {"flags": 8}, {"flags": 0, "split": 1}, {"flags": 0, "split": 5},
-                                 {"flags": 4}, {"flags": 6}, {"flags": 1}])
+# launch flags: 0 three-warpgroup kernel (default); 16 persistent kernel
+# (one CTA per SM taking work items); 4 two-tile kernel (+2: half its
+# exponentials on the FMA pipe); 1 one-tile kernel.  split: heads per
+# scheduling group.
+@pytest.mark.parametrize("cfg", [{"flags": 0}, {"flags": 0, "split": 1}, {"flags": 0, "split": 5}, {"flags": 16},
+                                 {"flags": 16, "split": 3}, {"flags": 4}, {"flags": 6}, {"flags": 1}])
 @pytest.mark.parametrize("causal,T,S,D", [(True, 1000, 1000, 128), (False, 130, 517, 128), (True, 700, 700, 64)])
 def test_kernel_variants(cfg, causal, T, S, D, cuda_device):
     check(2, 3, T, S, D, causal, torch.bfloat16, cuda_device, cfg=cfg)

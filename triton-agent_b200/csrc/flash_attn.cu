@@ -27,6 +27,8 @@
 // multicast is used.
 #include <math.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -1092,6 +1094,389 @@ __global__ void __launch_bounds__(kThreads3, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent kernel (flags bit 4): one CTA per SM takes work items -- a pair of
+// 128-row query tiles of one head -- from a global counter, in the
+// head-grouped, heaviest-first order of the three-warpgroup kernel, whose
+// warp roles, TMEM layout, K/V ring and register split it keeps.
+// Consecutive items overlap: the next item's Q tiles load once the last S
+// MMA of the current item has read Q (q_empty), its first S MMAs run while
+// the softmax warpgroups drain O, and only the first PV MMA of each tile
+// waits for that drain (o_empty).  Item ids pass from the producer thread
+// to the other roles through a two-slot queue in shared memory; every
+// barrier's phase runs on across items.
+// ---------------------------------------------------------------------------
+constexpr int kSchedSlots = 64;
+__device__ unsigned g_flash_sched[kSchedSlots];  // per-launch work counters (host zeroes one per launch)
+
+// work item lin -> (head bh, query-tile pair ct): heads in groups of
+// p.head_group; within a group the heaviest tile pairs of all its heads first
+__device__ __forceinline__ void flash_item(const FlashParams& p, int n_ct, int64_t lin, int& bh, int& ct) {
+  const int64_t BH = p.B * p.H;
+  const int64_t grp = lin / ((int64_t)p.head_group * n_ct);
+  const int64_t rem = lin - grp * p.head_group * n_ct;
+  const int64_t gh = min((int64_t)p.head_group, BH - grp * p.head_group);
+  bh = (int)(grp * p.head_group + rem % gh);
+  ct = n_ct - 1 - (int)(rem / gh);
+}
+
+// key tiles of the two query tiles of pair ct (causal: up to the diagonal); n1 >= n0
+__device__ __forceinline__ void flash_kt(const FlashParams& p, int ct, int& n0, int& n1) {
+  const int n_all = (int)((p.S + kBN - 1) / kBN);
+  const int64_t q0 = (int64_t)ct * 2 * kBM;
+  n0 = p.causal ? min(n_all, (int)((q0 + kBM - 1) / kBN) + 1) : n_all;
+  n1 = p.causal ? min(n_all, (int)((q0 + 2 * kBM - 1) / kBN) + 1) : n_all;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads3, 1)
+    flash_fwd4_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                                 const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
+                                 float* __restrict__ lse, FlashParams p, unsigned* __restrict__ sched) {
+  using L = Flash3Smem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = sm100::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_ct = (int)((p.T + 2 * kBM - 1) / (2 * kBM));
+  const int64_t n_items = p.B * p.H * n_ct;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* ring_full = bars + 2;              // [kRing3]
+  uint64_t* ring_empty = ring_full + kRing3;   // [kRing3]
+  uint64_t* s_full = ring_empty + kRing3;      // [2 tiles]
+  uint64_t* p_full = s_full + 2;               // [2 tiles]
+  uint64_t* o_full = s_full + 4;               // [2 tiles]
+  uint64_t* o_empty = s_full + 6;              // [2 tiles]
+  uint64_t* item_full = s_full + 8;            // [2 queue slots]
+  uint64_t* item_empty = s_full + 10;          // [2 queue slots]
+  int* item_q = reinterpret_cast<int*>(s_full + 12);  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_q + 2);
+  int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+  static_assert(2 + 2 * kRing3 + 12 <= 30, "barrier area");
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(sm100::smem_u32(q_full), 1);
+    sm100::mbar_init(sm100::smem_u32(q_empty), 1);
+    for (int i = 0; i < kRing3; ++i) {
+      sm100::mbar_init(sm100::smem_u32(&ring_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&ring_empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(sm100::smem_u32(&s_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&p_full[i]), 4);
+      sm100::mbar_init(sm100::smem_u32(&o_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&o_empty[i]), 4);
+      sm100::mbar_init(sm100::smem_u32(&item_full[i]), 1);
+      sm100::mbar_init(sm100::smem_u32(&item_empty[i]), 9);  // MMA thread + 8 softmax warps
+    }
+    *s_abort = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(sm100::smem_u32(tmem_slot), 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S_t at column 128 t, O_t at 256 + 128 t
+
+  if (warp < 4) {
+    sm100::setmaxnreg_dec<kRegsLow3>();
+    if (warp == 0 && lane == 0) {
+      // --------------------------------------------------- scheduler + producer
+      sm100::tma_prefetch_desc(&tm_q);
+      sm100::tma_prefetch_desc(&tm_k);
+      sm100::tma_prefetch_desc(&tm_v);
+      uint32_t rit = 0;  // ring items issued, over all work items
+      int q_issued = 0;  // Q loads issued (one per work item)
+      int k = 0;
+      bool ok = true;
+      for (;; ++k) {
+        const int qs = k & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&item_empty[qs]), ((k >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        const int64_t lin = *(volatile int*)s_abort ? n_items : (int64_t)atomicAdd(sched, 1u);
+        const int id = lin < n_items ? (int)lin : -1;
+        item_q[qs] = id;
+        sm100::mbar_arrive(sm100::smem_u32(&item_full[qs]));
+        if (id < 0) break;
+        int bh, ct, n0, n1;
+        flash_item(p, n_ct, id, bh, ct);
+        flash_kt(p, ct, n0, n1);
+        const int64_t q0 = (int64_t)ct * 2 * kBM;
+        if (k > 0 && !sm100::mbar_wait(sm100::smem_u32(q_empty), (k - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        const uint32_t qb = sm100::smem_u32(q_full);
+        sm100::mbar_arrive_expect_tx(qb, 2 * L::kTile);
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int h = 0; h < D / 64; ++h)
+            sm100::tma_load_3d(sbase + (t ? L::oQB : L::oQA) + h * L::kHalf, &tm_q, qb, h * 64,
+                               (int32_t)(q0 + t * kBM), bh);
+        ++q_issued;
+        for (int it = 0; it < 2 * n1; ++it, ++rit) {
+          const int slot = rit % kRing3;
+          if (!sm100::mbar_wait(sm100::smem_u32(&ring_empty[slot]), ((rit / kRing3) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = sm100::smem_u32(&ring_full[slot]);
+          sm100::mbar_arrive_expect_tx(fb, L::kTile);
+#pragma unroll
+          for (int h = 0; h < D / 64; ++h)
+            sm100::tma_load_3d(sbase + L::oRing + slot * L::kTile + h * L::kHalf, (it & 1) ? &tm_v : &tm_k, fb,
+                               h * 64, (it >> 1) * kBN, bh);
+        }
+        if (!ok) break;
+      }
+      if (!ok) {
+        b200_dev_error(kDevErrTimeoutEmpty);
+        atomicExch(s_abort, 1);
+      }
+      // no copy may still be writing shared memory when the CTA exits
+      if (q_issued > 0 && !sm100::mbar_wait(sm100::smem_u32(q_full), (q_issued - 1) & 1))
+        b200_dev_error(kDevErrTimeoutFull);
+      for (uint32_t it = rit > kRing3 ? rit - kRing3 : 0; it < rit; ++it)
+        if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[it % kRing3]), (it / kRing3) & 1))
+          b200_dev_error(kDevErrTimeoutFull);
+    } else if (warp == 1 && lane == 0) {
+      // ----------------------------------------------------------- MMA issue
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_s = sm100::make_idesc(1, fmt, fmt, 0, 0, kBM, kBN);
+      constexpr uint32_t idesc_o = sm100::make_idesc(1, fmt, fmt, 0, 1, kBM, D);
+      uint32_t rbase = 0;          // ring item of K_0 of the current work item
+      uint32_t pc0 = 0, pc1 = 0;   // P releases consumed per tile
+      bool ok = true;
+      auto ring_wait = [&](uint32_t it) -> uint32_t {
+        const uint32_t slot = it % kRing3;
+        if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[slot]), (it / kRing3) & 1)) return 0u;
+        sm100::tc_fence_after();
+        return sbase + L::oRing + slot * L::kTile;
+      };
+      auto release = [&](uint32_t it) { sm100::tc_commit(sm100::smem_u32(&ring_empty[it % kRing3])); };
+      auto issue_s = [&](int t, int j) -> bool {
+        const uint32_t kbase = ring_wait(rbase + 2 * j);
+        if (!kbase) return false;
+        const uint32_t qbase = sbase + (t ? L::oQB : L::oQA);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kHalf + (kk & 3) * 32;
+          const uint64_t ad = sm100::make_smem_desc(qbase + off, 16, 1024, sm100::kSwizzle128B);
+          const uint64_t bd = sm100::make_smem_desc(kbase + off, 16, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ss(tmem + t * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        sm100::tc_commit(sm100::smem_u32(&s_full[t]));
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!sm100::mbar_wait(sm100::smem_u32(&p_full[t]), (t ? pc1 : pc0) & 1)) return false;
+        if (t) ++pc1; else ++pc0;
+        const uint32_t vbase = ring_wait(rbase + 2 * j + 1);
+        if (!vbase) return false;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = sm100::make_smem_desc(vbase + kk * 2048, L::kHalf, 1024, sm100::kSwizzle128B);
+          sm100::mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        return true;
+      };
+      for (int k = 0; ok; ++k) {
+        const int qs = k & 1;
+        if (!sm100::mbar_wait(sm100::smem_u32(&item_full[qs]), (k >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        const int id = *(volatile int*)&item_q[qs];
+        sm100::mbar_arrive(sm100::smem_u32(&item_empty[qs]));
+        if (id < 0) break;
+        int bh, ct, n0, n1;
+        flash_item(p, n_ct, id, bh, ct);
+        flash_kt(p, ct, n0, n1);
+        if (!sm100::mbar_wait(sm100::smem_u32(q_full), k & 1)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        for (int t = 0; t < 2 && ok; ++t) ok = issue_s(t, 0);
+        if (!ok) break;
+        release(rbase);  // K_0
+        if (n1 == 1) sm100::tc_commit(sm100::smem_u32(q_empty));
+        for (int j = 0; ok && j < n1; ++j) {
+          if (*(volatile int*)s_abort) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            const int nkt = t ? n1 : n0;
+            if (j >= nkt) continue;
+            // O_t of the previous work item must be drained before PV_t(0) overwrites it
+            if (j == 0 && k > 0 && !sm100::mbar_wait(sm100::smem_u32(&o_empty[t]), (k - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            ok = issue_pv(t, j);
+            if (ok && t == 1) release(rbase + 2 * j + 1);  // V_j: tile B reads it last
+            if (ok && j + 1 < nkt) {
+              ok = issue_s(t, j + 1);
+              // the last S MMA of the item (tile B's, as n1 >= n0) frees Q
+              if (ok && t == 1 && j + 2 == n1) sm100::tc_commit(sm100::smem_u32(q_empty));
+            }
+            if (ok && j + 1 == nkt) sm100::tc_commit(sm100::smem_u32(&o_full[t]));
+          }
+          if (ok && j + 1 < n1) release(rbase + 2 * j + 2);  // K_{j+1}
+        }
+        rbase += 2 * n1;
+      }
+      if (!ok) {
+        b200_dev_error(kDevErrTimeoutFull);
+        atomicExch(s_abort, 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------ softmax + epilogue
+    sm100::setmaxnreg_inc<kRegsHigh3>();
+    const int t = (warp >> 2) - 1;  // tile of this warpgroup
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tSt = tmem + t * 128 + lane_off, tOt = tmem + 256 + t * 128 + lane_off;
+    uint32_t sc = 0;  // S_t tiles consumed
+    bool ok = true;
+    for (int k = 0;; ++k) {
+      const int qs = k & 1;
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&item_full[qs]), (k >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const int id = *(volatile int*)&item_q[qs];
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&item_empty[qs]));
+      if (id < 0) break;
+      int bh, ct, n0, n1;
+      flash_item(p, n_ct, id, bh, ct);
+      flash_kt(p, ct, n0, n1);
+      const int nj = t ? n1 : n0;
+      const int64_t qrow = (int64_t)ct * 2 * kBM + t * kBM + r;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nj; ++j, ++sc) {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&s_full[t]), sc & 1)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        uint32_t v[kBN];
+        sm100::tmem_ld_32x32b_x64(tSt, v);
+        sm100::tmem_ld_32x32b_x64(tSt + 64, v + 64);
+        sm100::tmem_wait_ld();
+        const int64_t k0 = (int64_t)j * kBN;
+        int valid = kBN;
+        if ((k0 + kBN > p.S) || (p.causal && k0 + kBN - 1 > qrow)) {
+          const int64_t lim = (p.causal && qrow + 1 < p.S) ? qrow + 1 : p.S;
+          const int64_t nv = lim - k0;
+          valid = nv <= 0 ? 0 : (nv >= kBN ? kBN : (int)nv);
+        }
+        if (!__all_sync(0xffffffffu, valid == kBN)) {
+#pragma unroll
+          for (int i = 0; i < kBN; ++i)
+            if (i >= valid) v[i] = 0xff800000u;  // -inf: max ignores it, 2^-inf = 0
+        }
+        float mx4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kBN; i += 8) {
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+            mx4[a] = sm100::fmax3(mx4[a], __uint_as_float(v[i + 2 * a]), __uint_as_float(v[i + 2 * a + 1]));
+        }
+        const float mx = sm100::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * p.sl2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (m_used == -INFINITY) {
+          m_used = mx;
+        } else if (mx > m_used + kRescaleThreshold) {
+          alpha = ex2_approx(m_used - mx);
+          m_used = mx;
+          rescale = true;
+        }
+        const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+        const float rs = softmax_row_to_tmem<T, 0>(v, p.sl2, neg_m, tSt);
+        // O_t holds PV_t(j-1), complete because S_t(j) is: rescale it if the
+        // max moved (before P_t(j) is released to the MMA)
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            sm100::tmem_ld_32x32b_x32(tOt + c, o);
+            sm100::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              float y0, y1;
+              sm100::fmul2_bcast(y0, y1, __uint_as_float(o[i]), __uint_as_float(o[i + 1]), alpha);
+              o[i] = __float_as_uint(y0);
+              o[i + 1] = __float_as_uint(y1);
+            }
+            sm100::tmem_st_32x32b_x32(tOt + c, o);
+          }
+        }
+        sm100::tmem_wait_st();
+        l = l * alpha + rs;
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&p_full[t]));
+      }
+      if (!ok) break;
+      // epilogue: read O_t out of tensor memory, hand it back to the MMA,
+      // then O_t / l to global memory
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&o_full[t]), k & 1)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      uint32_t o[D];
+#pragma unroll
+      for (int c = 0; c < D; c += 32) sm100::tmem_ld_32x32b_x32(tOt + c, o + c);
+      sm100::tmem_wait_ld();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&o_empty[t]));
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      if (qrow < p.T) {
+        T* orow = out + ((int64_t)bh * p.T + qrow) * D;
+#pragma unroll
+        for (int c = 0; c < D; c += 8) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[c + 0]) * inv, __uint_as_float(o[c + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c) = w;
+        }
+        if (p.out_lse) lse[(int64_t)bh * p.T + qrow] = (m_used + log2f(l)) * 0.6931471805599453f;
+      }
+    }
+    if (!ok) {
+      b200_dev_error(kDevErrTimeoutMma);
+      atomicExch(s_abort, 1);
+    }
+    sm100::tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // General fallback for head dims the tensor-core path does not cover (<= 256):
 // one warp per query row, lanes over keys, fp32 online softmax.
 // ---------------------------------------------------------------------------
@@ -1164,6 +1549,37 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse, 
     st = encode_tensor_map(&tv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
+  if (variant == 4) {
+    auto kern = flash_fwd4_persistent_kernel<T, D>;
+    const int smem = (int)Flash3Smem<D>::kTotal;
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return launch_status(e);
+    // the softmax warpgroups' setmaxnreg.inc draws on the launch registers
+    if (fa.numRegs < kRegsLaunch3) {
+      variant = 3;
+    } else {
+      const int64_t n_items = p.B * p.H * ((p.T + 2 * kBM - 1) / (2 * kBM));
+      if (n_items > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
+      int dev = 0, sms = 0;
+      if ((e = cudaGetDevice(&dev)) != cudaSuccess) return launch_status(e);
+      if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return launch_status(e);
+      unsigned* counters = nullptr;
+      if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&counters), g_flash_sched)) != cudaSuccess)
+        return launch_status(e);
+      // one counter per launch, round-robin over the slots, so launches on
+      // different streams do not share a counter unless kSchedSlots are in flight
+      static std::atomic<unsigned> seq{0};
+      unsigned* sched = counters + (seq.fetch_add(1, std::memory_order_relaxed) % kSchedSlots);
+      if ((e = cudaMemsetAsync(sched, 0, sizeof(unsigned), s)) != cudaSuccess) return launch_status(e);
+      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+        return launch_status(e);
+      const unsigned grid = (unsigned)(n_items < sms ? n_items : sms);
+      kern<<<grid, kThreads3, smem, s>>>(tq, tk, tv, static_cast<T*>(o), lse, p, sched);
+      return launch_status(cudaGetLastError());
+    }
+  }
   if (variant == 3) {
     auto kern = flash_fwd3_tcgen05_kernel<T, D>;
     const int smem = (int)Flash3Smem<D>::kTotal;
@@ -1233,9 +1649,10 @@ extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void
   if (tc) {
     return B200_DISPATCH_HALF(dtype, [&] {
       // flags bit 0: the one-tile kernel (P staged in shared memory);
-      // bit 2: the two-tile kernel without register reallocation
+      // bit 2: the two-tile kernel without register reallocation; bit 4:
+      // the persistent kernel (one CTA per SM taking work items)
       const int fl = cfg ? cfg->flags : 0;
-      const int variant = (fl & 1) ? 1 : (fl & 4) ? 2 : 3;
+      const int variant = (fl & 1) ? 1 : (fl & 4) ? 2 : (fl & 16) ? 4 : 3;
       return D == 128 ? launch_tc<scalar_t, 128>(q, k, v, o, lse, p, variant, s)
                       : launch_tc<scalar_t, 64>(q, k, v, o, lse, p, variant, s);
     });
