@@ -37,10 +37,18 @@ def test_int8_gemm_out_dtypes(out_dtype, cuda_device):
     check(200, 384, 512, cuda_device, out_dtype=out_dtype)
 
 
-@pytest.mark.parametrize("cfg", [{"tile_n": 128}, {"tile_n": 256}, {"split": 4}, {"stages": 2},
-                                 {"tile_n": 128, "split": 3, "stages": 3}])
+# flags bit 1 selects the one-SM persistent kernel over the CTA-pair kernel
+# (the default for M > 128); tile_n applies to the one-SM kernel
+@pytest.mark.parametrize("cfg", [{"flags": 2, "tile_n": 128}, {"flags": 2, "tile_n": 256}, {"split": 4},
+                                 {"stages": 2}, {"flags": 2, "stages": 3}, {"tile_n": 128, "split": 3, "stages": 3}])
 def test_int8_gemm_configs(cfg, cuda_device):
     check(256, 768, 2048, cuda_device, cfg=cfg)
+
+
+@pytest.mark.parametrize("M,N,K_", [(600, 1000, 640), (257, 300, 128), (129, 256, 4128), (1024, 4096, 48)])
+def test_int8_gemm_pair_kernel_tails(M, N, K_, cuda_device):
+    """CTA-pair kernel: several 256 x 256 tiles per pair, ragged M, N and K."""
+    check(M, N, K_, cuda_device)
 
 
 def test_int8_gemm_baseline_shapes_checksum(cuda_device):

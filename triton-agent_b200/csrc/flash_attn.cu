@@ -908,49 +908,67 @@ __global__ void __launch_bounds__(kThreads3, 1)
       for (int it = issued - 1; it >= 0 && it >= issued - kRing3; --it)
         if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[it % kRing3]), (it / kRing3) & 1))
           b200_dev_error(kDevErrTimeoutFull);
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
       // ----------------------------------------------------------- MMA issue
+      // The whole warp runs the loop (waits, descriptors and ring position
+      // stay warp-uniform); one elected lane issues the MMAs and commits.
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_s = sm100::make_idesc(1, fmt, fmt, 0, 0, kBM, kBN);
       constexpr uint32_t idesc_o = sm100::make_idesc(1, fmt, fmt, 0, 1, kBM, D);
-      bool ok = sm100::mbar_wait(sm100::smem_u32(q_full), 0);
-      auto ring_wait = [&](int it) -> uint32_t {
-        const int slot = it % kRing3;
-        if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[slot]), (it / kRing3) & 1)) return 0u;
-        sm100::tc_fence_after();
-        return sbase + L::oRing + slot * L::kTile;
+      const uint32_t leader = sm100::elect_one();
+      // Descriptors at offset 0; a ring slot or K step adds its byte offset
+      // >> 4 to the start-address field (bits [0,14)), which never carries
+      // since shared addresses stay below 2^18.
+      const uint64_t dq0 = sm100::make_smem_desc(sbase + L::oQA, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t dq1 = sm100::make_smem_desc(sbase + L::oQB, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t dk = sm100::make_smem_desc(sbase + L::oRing, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t dv = sm100::make_smem_desc(sbase + L::oRing, L::kHalf, 1024, sm100::kSwizzle128B);
+      bool ok = sm100::mbar_wait_warp(sm100::smem_u32(q_full), 0);
+      // ring position of item it = 2j (K_j) or 2j + 1 (V_j): slot it % kRing3,
+      // phase (it / kRing3) & 1 -- kept incrementally for the next K and V
+      int k_slot = 0, v_slot = 1;
+      uint32_t k_ph = 0, v_ph = 0;
+      auto adv2 = [](int& slot, uint32_t& ph) {
+        slot += 2;
+        if (slot >= kRing3) {
+          slot -= kRing3;
+          ph ^= 1u;
+        }
       };
-      auto release = [&](int it) { sm100::tc_commit(sm100::smem_u32(&ring_empty[it % kRing3])); };
-      auto issue_s = [&](int t, int j) -> bool {
-        const uint32_t kbase = ring_wait(2 * j);
-        if (!kbase) return false;
-        const uint32_t qbase = sbase + (t ? L::oQB : L::oQA);
+      auto issue_s = [&](int t, int slot, uint32_t ph) -> bool {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&ring_full[slot]), ph)) return false;
+        sm100::tc_fence_after();
+        const uint64_t ad = t ? dq1 : dq0;
+        const uint64_t bd = dk + (uint64_t)((slot * L::kTile) >> 4);
+        const uint32_t d_tmem = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kHalf + (kk & 3) * 32;
-          const uint64_t ad = sm100::make_smem_desc(qbase + off, 16, 1024, sm100::kSwizzle128B);
-          const uint64_t bd = sm100::make_smem_desc(kbase + off, 16, 1024, sm100::kSwizzle128B);
-          sm100::mma_f16_ss(tmem + t * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * L::kHalf + (kk & 3) * 32) >> 4;
+          sm100::mma_f16_ss(d_tmem, ad + off, bd + off, idesc_s, kk > 0 ? 1u : 0u, leader);
         }
-        sm100::tc_commit(sm100::smem_u32(&s_full[t]));
+        sm100::tc_commit(sm100::smem_u32(&s_full[t]), leader);
         return true;
       };
-      auto issue_pv = [&](int t, int j) -> bool {
-        if (!sm100::mbar_wait(sm100::smem_u32(&p_full[t]), j & 1)) return false;
-        const uint32_t vbase = ring_wait(2 * j + 1);
-        if (!vbase) return false;
+      auto issue_pv = [&](int t, int j, int slot, uint32_t ph) -> bool {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&p_full[t]), j & 1)) return false;
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&ring_full[slot]), ph)) return false;
+        sm100::tc_fence_after();
+        const uint64_t bd = dv + (uint64_t)((slot * L::kTile) >> 4);
+        const uint32_t d_tmem = tmem + 256 + t * 128, a_tmem = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           // V: MN-major; 16 keys = two 8-row groups of 128 B (SBO 1024),
           // head-dim halves one box (16 KB) apart (LBO).  P: 8 TMEM columns
           // of bf16 pairs per 16 keys.
-          const uint64_t bd = sm100::make_smem_desc(vbase + kk * 2048, L::kHalf, 1024, sm100::kSwizzle128B);
-          sm100::mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          sm100::mma_f16_ts(d_tmem, a_tmem + kk * 8, bd + (uint64_t)((kk * 2048) >> 4), idesc_o,
+                            (j > 0 || kk > 0) ? 1u : 0u, leader);
         }
         return true;
       };
-      for (int t = 0; t < 2 && ok; ++t) ok = issue_s(t, 0);
-      if (ok) release(0);  // K_0
+      auto release = [&](int slot) { sm100::tc_commit(sm100::smem_u32(&ring_empty[slot]), leader); };
+      for (int t = 0; t < 2 && ok; ++t) ok = issue_s(t, k_slot, k_ph);
+      if (ok) release(k_slot);  // K_0
+      adv2(k_slot, k_ph);       // -> K_1
       for (int j = 0; ok && j < n_kt_max; ++j) {
         if (*(volatile int*)s_abort) {
           ok = false;
@@ -959,17 +977,21 @@ __global__ void __launch_bounds__(kThreads3, 1)
         for (int t = 0; t < 2 && ok; ++t) {
           const int nkt = t ? n_kt1 : n_kt0;
           if (j >= nkt) continue;
-          ok = issue_pv(t, j);
-          if (ok && t == 1) release(2 * j + 1);  // V_j: tile B reads it last
-          if (ok && j + 1 < nkt) ok = issue_s(t, j + 1);
-          if (ok && j + 1 == nkt) sm100::tc_commit(sm100::smem_u32(&o_done[t]));
+          ok = issue_pv(t, j, v_slot, v_ph);
+          if (ok && t == 1) release(v_slot);  // V_j: tile B reads it last
+          if (ok && j + 1 < nkt) ok = issue_s(t, k_slot, k_ph);
+          if (ok && j + 1 == nkt) sm100::tc_commit(sm100::smem_u32(&o_done[t]), leader);
         }
-        if (ok && j + 1 < n_kt_max) release(2 * j + 2);  // K_{j+1}
+        if (ok && j + 1 < n_kt_max) release(k_slot);  // K_{j+1}
+        adv2(k_slot, k_ph);
+        adv2(v_slot, v_ph);
       }
       if (!ok) {
-        b200_dev_error(kDevErrTimeoutFull);
-        atomicExch(s_abort, 1);
-        for (int t = 0; t < 2; ++t) sm100::tc_commit(sm100::smem_u32(&o_done[t]));
+        if (leader) {
+          b200_dev_error(kDevErrTimeoutFull);
+          atomicExch(s_abort, 1);
+        }
+        for (int t = 0; t < 2; ++t) sm100::tc_commit(sm100::smem_u32(&o_done[t]), leader);
       }
     }
   } else {

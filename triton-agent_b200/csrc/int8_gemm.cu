@@ -141,15 +141,29 @@ __device__ __forceinline__ void set_abort(const Bars& b, int code) {
   atomicExch(&b.flags[0], 1);
 }
 
+// Position in the ring of stages: stage index and fill phase, advanced
+// without divisions (they sit on the issue path of a single thread).
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int stages) {
+    if (++s == stages) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
 // Producer: streams `count` stages of {first operand box at (kx, r0), second
 // at (kx, r1)} for k tiles [kt0, kt0 + count), continuing the ring position
-// `it`.  Returns false if a wait timed out.
+// `r` (`it` counts fills, for the final drain).  Returns false if a wait
+// timed out.
 __device__ __forceinline__ bool produce(const CUtensorMap* ta, const CUtensorMap* tb, const Bars& bars,
                                         uint32_t base, const GemmParams& p, int kt0, int count, int32_t r0,
-                                        int32_t r1, int& it) {
-  for (int i = 0; i < count; ++i, ++it) {
-    const int s = it % p.stages;
-    if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[s]), ((it / p.stages) & 1) ^ 1)) return false;
+                                        int32_t r1, Ring& r, int& it) {
+  for (int i = 0; i < count; ++i, ++it, r.next(p.stages)) {
+    const int s = r.s;
+    if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[s]), r.ph ^ 1u)) return false;
     if (aborted(bars)) return false;
     const uint32_t fb = sm100::smem_u32(&bars.full[s]);
     sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
@@ -169,28 +183,29 @@ __device__ __forceinline__ void drain_fills(const Bars& bars, const GemmParams& 
       b200_dev_error(kDevErrTimeoutFull);
 }
 
-// MMA issue of `count` stages into accumulator `d_tmem`; returns false on timeout.
+// MMA issue of `count` stages into accumulator `d_tmem`, run by a whole warp
+// (waits, descriptors and ring position warp-uniform); the lane with
+// `leader` set issues the MMAs and commits.  Returns false on timeout.
 template <int N_MMA>
 __device__ __forceinline__ bool mma_stages(const Bars& bars, uint32_t base, const GemmParams& p, uint32_t d_tmem,
-                                           int count, int& it) {
+                                           int count, Ring& r, uint32_t leader) {
   constexpr uint32_t idesc = sm100::make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, 0, 0, BM, N_MMA);
-  for (int i = 0; i < count; ++i, ++it) {
-    const int s = it % p.stages;
-    if (!sm100::mbar_wait(sm100::smem_u32(&bars.full[s]), (it / p.stages) & 1)) return false;
+  // K-major SWIZZLE_128B: 8-row atoms of 1024 B stacked along M/N (SBO =
+  // 1024); stepping K by 32 bytes inside the atom moves the start address,
+  // the hardware applies the swizzle.  Descriptors of stage 0; a stage or K
+  // step adds its byte offset >> 4 to the start-address field (bits
+  // [0,14)), which never carries since shared addresses stay below 2^18.
+  const uint64_t ad0 = sm100::make_smem_desc(base, 16, 1024, sm100::kSwizzle128B);
+  const uint64_t bd0 = sm100::make_smem_desc(base + p.a_bytes, 16, 1024, sm100::kSwizzle128B);
+  for (int i = 0; i < count; ++i, r.next(p.stages)) {
+    if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.full[r.s]), r.ph)) return false;
     if (aborted(bars)) return false;
     sm100::tc_fence_after();
-    const uint32_t a_base = base + s * p.stage_bytes;
-    const uint32_t b_base = a_base + p.a_bytes;
+    const uint64_t so = (uint64_t)((r.s * p.stage_bytes) >> 4);
 #pragma unroll
-    for (int kk = 0; kk < BK / 32; ++kk) {
-      // K-major SWIZZLE_128B: 8-row atoms of 1024 B stacked along M/N
-      // (SBO = 1024); stepping K by 32 bytes inside the atom moves the start
-      // address, the hardware applies the swizzle.
-      const uint64_t ad = sm100::make_smem_desc(a_base + kk * 32, 16, 1024, sm100::kSwizzle128B);
-      const uint64_t bd = sm100::make_smem_desc(b_base + kk * 32, 16, 1024, sm100::kSwizzle128B);
-      sm100::mma_i8_ss(d_tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-    }
-    sm100::tc_commit(sm100::smem_u32(&bars.empty[s]));
+    for (int kk = 0; kk < BK / 32; ++kk)
+      sm100::mma_i8_ss(d_tmem, ad0 + so + 2 * kk, bd0 + so + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u, leader);
+    sm100::tc_commit(sm100::smem_u32(&bars.empty[r.s]), leader);
   }
   return true;
 }
@@ -238,9 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tma_prefetch_desc(&tm_a);
       sm100::tma_prefetch_desc(&tm_b);
       int it = 0;
+      Ring r;
       for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
         const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
-        if (!produce(&tm_a, &tm_b, bars, base, p, 0, p.k_tiles, m_tile * BM, n_tile * BN, it)) {
+        if (!produce(&tm_a, &tm_b, bars, base, p, 0, p.k_tiles, m_tile * BM, n_tile * BN, r, it)) {
           set_abort(bars, kDevErrTimeoutEmpty);
           break;
         }
@@ -248,25 +264,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_fills(bars, p, it);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      int it = 0, lt = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++lt) {
-        const int a = lt & 1;
-        // the epilogue must have drained this accumulator (tile lt - 2)
-        if (!sm100::mbar_wait(sm100::smem_u32(&bars.acc_empty[a]), ((lt >> 1) & 1) ^ 1)) {
-          ok = false;
-          break;
-        }
-        sm100::tc_fence_after();
-        ok = mma_stages<BN>(bars, base, p, tmem + a * BN, p.k_tiles, it);
-        sm100::tc_commit(sm100::smem_u32(&bars.acc_full[a]));
+    // MMA issue: the whole warp runs the loop, one elected lane issues
+    const uint32_t leader = sm100::elect_one();
+    Ring r;
+    int lt = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++lt) {
+      const int a = lt & 1;
+      // the epilogue must have drained this accumulator (tile lt - 2)
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_empty[a]), ((lt >> 1) & 1) ^ 1)) {
+        ok = false;
+        break;
       }
-      if (!ok) set_abort(bars, kDevErrTimeoutFull);
-      // every issued MMA has completed before TMEM is released
-      sm100::tc_commit(sm100::smem_u32(bars.mma_done));
-      if (!sm100::mbar_wait(sm100::smem_u32(bars.mma_done), 0)) b200_dev_error(kDevErrTimeoutMma);
+      sm100::tc_fence_after();
+      ok = mma_stages<BN>(bars, base, p, tmem + a * BN, p.k_tiles, r, leader);
+      sm100::tc_commit(sm100::smem_u32(&bars.acc_full[a]), leader);
     }
+    if (!ok && leader) set_abort(bars, kDevErrTimeoutFull);
+    // every issued MMA has completed before TMEM is released
+    sm100::tc_commit(sm100::smem_u32(bars.mma_done), leader);
+    if (!sm100::mbar_wait_warp(sm100::smem_u32(bars.mma_done), 0) && leader) b200_dev_error(kDevErrTimeoutMma);
   } else {
     const int quarter = warp & 3;
     int lt = 0;
@@ -297,6 +314,170 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Pair kernel (M > 128): a cluster of two CTAs on two SMs computes 256 x 256
+// output tiles with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).
+// Each CTA streams only its own 128 rows of A and 128 rows of W per stage
+// (32 KB, where a 128 x 256 tile on one SM streams 48 KB), which cuts the
+// L2 -> shared-memory traffic per MMA by a third.  Both CTAs: warp 0 TMA
+// producer, warps 2..5 epilogue of the CTA's 128 accumulator rows (TMEM is
+// allocated pair-wide, 2 x 256 columns).  Rank 0 only: warp 1 issues the
+// pair MMAs.  Fills of both CTAs complete on rank 0's full barriers (rank 0
+// expects both CTAs' bytes); rank 0 commits MMA progress to the empty and
+// accumulator barriers of both CTAs, and both epilogues arrive on rank 0's
+// acc_empty.  No multicast anywhere: every load reads global memory into
+// the issuing CTA's own shared memory.
+// ----------------------------------------------------------------------------
+constexpr int kPairN = 256;
+
+template <typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                          const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
+                          int32_t* __restrict__ acc_out, GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();
+  const int pair = (int)(blockIdx.x >> 1), n_pairs = (int)(gridDim.x >> 1);
+  const Bars bars = carve(smem, p);
+  const uint32_t base = sm100::smem_u32(smem);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      sm100::mbar_init(sm100::smem_u32(&bars.full[s]), 1);
+      sm100::mbar_init(sm100::smem_u32(&bars.empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(sm100::smem_u32(&bars.acc_full[a]), 1);
+      sm100::mbar_init(sm100::smem_u32(&bars.acc_empty[a]), 8);  // 4 epilogue warps in each CTA
+    }
+    sm100::mbar_init(sm100::smem_u32(bars.mma_done), 1);
+    bars.flags[0] = 0;
+    bars.flags[1] = 0;
+    sm100::fence_barrier_init();
+  }
+  // both CTAs' barriers exist before either CTA signals the other's
+  sm100::cluster_sync();
+  if (warp == 1) {
+    sm100::tmem_alloc_pair(sm100::smem_u32(bars.tmem_slot), 2 * kPairN);
+    sm100::tmem_relinquish_pair();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *bars.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_a);
+      sm100::tma_prefetch_desc(&tm_b);
+      int it = 0;
+      Ring r;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += n_pairs) {
+        const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
+        const int32_t a_row = m_tile * 2 * BM + (int32_t)rank * BM;
+        const int32_t b_row = n_tile * kPairN + (int32_t)rank * (kPairN / 2);
+        for (int kt = 0; kt < p.k_tiles; ++kt, ++it, r.next(p.stages)) {
+          const int s = r.s;
+          if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[s]), r.ph ^ 1u) || aborted(bars)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = sm100::smem_u32(&bars.full[s]);
+          if (rank == 0) sm100::mbar_arrive_expect_tx(fb, 2 * p.stage_bytes);  // both CTAs' fills
+          const uint32_t fb0 = sm100::mapa_shared(fb, 0);
+          const uint32_t dst = base + s * p.stage_bytes;
+          sm100::tma_load_2d_pair(dst, &tm_a, fb0, kt * BK, a_row);
+          sm100::tma_load_2d_pair(dst + p.a_bytes, &tm_b, fb0, kt * BK, b_row);
+        }
+      }
+      if (!ok) set_abort(bars, kDevErrTimeoutEmpty);
+      // rank 0's full barriers count both CTAs' bytes: its drain covers the pair
+      if (rank == 0) drain_fills(bars, p, it);
+    }
+  } else if (warp == 1) {
+    if (rank == 0) {
+      // MMA issue for the pair: the whole warp runs the loop, one elected lane issues
+      constexpr uint32_t idesc = sm100::make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, 0, 0, 2 * BM, kPairN);
+      const uint32_t leader = sm100::elect_one();
+      const uint64_t ad0 = sm100::make_smem_desc(base, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t bd0 = sm100::make_smem_desc(base + p.a_bytes, 16, 1024, sm100::kSwizzle128B);
+      const uint32_t empty0 = sm100::smem_u32(&bars.empty[0]);
+      const uint32_t empty_r0 = sm100::mapa_shared(empty0, 0), empty_r1 = sm100::mapa_shared(empty0, 1);
+      const uint32_t accf0 = sm100::smem_u32(&bars.acc_full[0]);
+      const uint32_t accf_r0 = sm100::mapa_shared(accf0, 0), accf_r1 = sm100::mapa_shared(accf0, 1);
+      Ring r;
+      int lt = 0;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += n_pairs, ++lt) {
+        const int a = lt & 1;
+        // both epilogues must have drained this accumulator (tile lt - 2)
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_empty[a]), ((lt >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem + a * kPairN;
+        for (int kt = 0; kt < p.k_tiles; ++kt, r.next(p.stages)) {
+          if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.full[r.s]), r.ph) || aborted(bars)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint64_t so = (uint64_t)((r.s * p.stage_bytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            sm100::mma_i8_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u,
+                                  leader);
+          sm100::tc_commit_pair(empty_r0 + 8 * r.s, leader);
+          sm100::tc_commit_pair(empty_r1 + 8 * r.s, leader);
+        }
+        if (!ok) break;
+        sm100::tc_commit_pair(accf_r0 + 8 * a, leader);
+        sm100::tc_commit_pair(accf_r1 + 8 * a, leader);
+      }
+      if (!ok && leader) set_abort(bars, kDevErrTimeoutFull);
+      // every issued MMA has completed before TMEM is released
+      sm100::tc_commit_pair(sm100::mapa_shared(sm100::smem_u32(bars.mma_done), 0), leader);
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(bars.mma_done), 0) && leader) b200_dev_error(kDevErrTimeoutMma);
+    }
+  } else {
+    const int quarter = warp & 3;
+    int lt = 0;
+    const uint32_t acc_empty0 = sm100::mapa_shared(sm100::smem_u32(&bars.acc_empty[0]), 0);
+    for (int t = pair; t < p.num_tiles; t += n_pairs, ++lt) {
+      const int a = lt & 1;
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_full[a]), (lt >> 1) & 1)) {
+        set_abort(bars, kDevErrTimeoutMma);
+        break;
+      }
+      sm100::tc_fence_after();
+      const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
+      const int64_t row = (int64_t)m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
+      const uint32_t t_row = tmem + a * kPairN + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kPairN; c += 32) {
+        uint32_t acc[32];
+        sm100::tmem_ld_32x32b_x32(t_row + c, acc);
+        sm100::tmem_wait_ld_regs(acc);
+        if (row < p.M && !aborted(bars))
+          epilogue_chunk<OutT>(acc, row, (int64_t)n_tile * kPairN + c, sA, sW, C, acc_out, p);
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive_cluster(acc_empty0 + a * 8);
+    }
+  }
+  __syncthreads();
+  // neither CTA leaves (or frees TMEM) while its peer may still signal it
+  sm100::cluster_sync();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc_pair(tmem, 2 * kPairN);
   }
 }
 
@@ -333,15 +514,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tma_prefetch_desc(&tm_w);
       sm100::tma_prefetch_desc(&tm_a);
       int it = 0;
-      if (!produce(&tm_w, &tm_a, bars, base, p, kt0, nk, n_tile * BM, 0, it)) set_abort(bars, kDevErrTimeoutEmpty);
+      Ring r;
+      if (!produce(&tm_w, &tm_a, bars, base, p, kt0, nk, n_tile * BM, 0, r, it))
+        set_abort(bars, kDevErrTimeoutEmpty);
       drain_fills(bars, p, it);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      int it = 0;
-      if (!mma_stages<MN>(bars, base, p, tmem, nk, it)) set_abort(bars, kDevErrTimeoutFull);
-      sm100::tc_commit(sm100::smem_u32(&bars.acc_full[0]));
-    }
+    const uint32_t leader = sm100::elect_one();
+    Ring r;
+    if (!mma_stages<MN>(bars, base, p, tmem, nk, r, leader) && leader) set_abort(bars, kDevErrTimeoutFull);
+    sm100::tc_commit(sm100::smem_u32(&bars.acc_full[0]), leader);
   } else {
     const int quarter = warp & 3;
     const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
@@ -414,6 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 struct GemmPlan {
   bool skinny;
+  bool pair;       // two-SM kernel (256 x 256 tiles per CTA pair)
+  int b_box_rows;  // rows of the second operand's TMA box
   int BN;  // persistent tile width, or MN (padded M) for skinny
   int splits, k_tiles, k_tiles_split, stages, m_tiles, n_tiles, grid;
   uint32_t stage_bytes, a_bytes;
@@ -442,6 +626,18 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
     g.stage_bytes = g.a_bytes + g.BN * BK;
     g.grid = g.n_tiles * g.splits;
     if (g.splits > 1) g.ws_bytes = kTicketBytes + (size_t)M * N * 4;
+  } else if (M > 128 && !(cfg && (cfg->flags & 2)) && sms >= 2) {  // flags bit 1: one-SM persistent kernel
+    g.pair = true;
+    g.BN = kPairN;
+    g.m_tiles = (int)((M + 2 * BM - 1) / (2 * BM));
+    g.n_tiles = (int)((N + kPairN - 1) / kPairN);
+    g.splits = 1;
+    g.k_tiles_split = g.k_tiles;
+    g.a_bytes = BM * BK;                  // this CTA's 128 rows of A
+    g.stage_bytes = g.a_bytes + (kPairN / 2) * BK;  // + its 128 rows of W
+    const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
+    const int pairs = sms / 2;
+    g.grid = 2 * (int)(tiles < pairs ? tiles : pairs);
   } else {
     int bn = (cfg && cfg->tile_n > 0) ? cfg->tile_n : 256;
     if (bn != 128 && bn != 256) bn = 256;
@@ -456,6 +652,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
     const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
     g.grid = (int)(tiles < sms ? tiles : sms);
   }
+  g.b_box_rows = g.skinny ? g.BN : (g.pair ? kPairN / 2 : g.BN);
   int stages = (cfg && cfg->stages > 0) ? cfg->stages : 8;
   while (stages > 2 && (size_t)stages * g.stage_bytes > budget) --stages;
   g.stages = stages;
@@ -466,6 +663,26 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
 template <typename OutT>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
            int32_t* acc_out, void* ws, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
+  if (g.pair) {
+    auto kern = int8_gemm_pair_kernel<OutT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+    if (e != cudaSuccess) return launch_status(e);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)g.grid);
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = g.smem;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&lc, kern, ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, p);
+    if (e != cudaSuccess) return launch_status(e);
+    return launch_status(cudaGetLastError());
+  }
   if (!g.skinny) {
     auto kern = g.BN == 256 ? int8_gemm_tcgen05_kernel<256, OutT> : int8_gemm_tcgen05_kernel<128, OutT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
@@ -534,7 +751,7 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)rows1};
     const uint64_t strides[1] = {(uint64_t)K};
-    const uint32_t box[2] = {BK, (uint32_t)g.BN};
+    const uint32_t box[2] = {BK, (uint32_t)g.b_box_rows};
     int st = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, op1, dims, strides, box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
