@@ -45,6 +45,16 @@ def test_int8_gemm_configs(cfg, cuda_device):
     check(256, 768, 2048, cuda_device, cfg=cfg)
 
 
+# small M: the streaming kernel (default; W cut into one k-range per SM) and
+# the split-grid kernel (flags bit 2), with ragged N and K and repeated calls
+# (the partial-sum workspace must come back to zero)
+@pytest.mark.parametrize("cfg", [None, {"flags": 4}, {"stages": 3}, {"flags": 4, "split": 3}])
+@pytest.mark.parametrize("M,N,K_", [(1, 300, 4096), (16, 1000, 1008), (33, 4096, 640), (64, 2000, 8192)])
+def test_int8_gemm_skinny_kernels(cfg, M, N, K_, cuda_device):
+    for seed in (0, 1):
+        check(M, N, K_, cuda_device, cfg=cfg, seed=seed)
+
+
 @pytest.mark.parametrize("M,N,K_", [(600, 1000, 640), (257, 300, 128), (129, 256, 4128), (1024, 4096, 48)])
 def test_int8_gemm_pair_kernel_tails(M, N, K_, cuda_device):
     """CTA-pair kernel: several 256 x 256 tiles per pair, ragged M, N and K."""

@@ -482,6 +482,172 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------
+// Streaming skinny kernel (M <= 64, default): the n_tiles x k_tiles W tiles
+// (128 rows x 128 B) are cut into one contiguous range per CTA, n-major and
+// k-minor, so every SM streams the same number of W bytes through one deep
+// TMA ring (one CTA per SM).  A range splits into segments (one n tile, a
+// run of its k tiles), accumulated alternately in two TMEM buffers.  A
+// segment spanning all of K is dequantised directly; any other red.adds its
+// exact int32 partial into the workspace and adds its k-tile count to the
+// n tile's ticket, and the CTA that completes the count dequantises the
+// tile and re-zeroes it (workspace and ticket) for the next call.
+// ----------------------------------------------------------------------------
+template <int MN, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    int8_gemm_stream_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                            const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
+                            int32_t* __restrict__ acc_out, int32_t* __restrict__ ws, int* __restrict__ tickets,
+                            GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Bars bars = carve(smem, p);
+  const uint32_t base = sm100::smem_u32(smem);
+  constexpr int kCols = MN < 32 ? 32 : MN;  // TMEM allocation granularity, per buffer
+  const int64_t U = (int64_t)p.n_tiles * p.k_tiles;
+  const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+  if (threadIdx.x == 0) init_bars(bars, p);
+  if (warp == 1) {
+    sm100::tmem_alloc(sm100::smem_u32(bars.tmem_slot), 2 * kCols);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *bars.tmem_slot;
+  const int n_first = (int)(u0 / p.k_tiles);
+  const int kt_first = (int)(u0 - (int64_t)n_first * p.k_tiles);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::tma_prefetch_desc(&tm_w);
+      sm100::tma_prefetch_desc(&tm_a);
+      int it = 0;
+      Ring r;
+      int n = n_first, kt = kt_first;
+      for (int64_t u = u0; u < u1; ++u, ++it, r.next(p.stages)) {
+        if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[r.s]), r.ph ^ 1u) || aborted(bars)) {
+          set_abort(bars, kDevErrTimeoutEmpty);
+          break;
+        }
+        const uint32_t fb = sm100::smem_u32(&bars.full[r.s]);
+        sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
+        const uint32_t dst = base + r.s * p.stage_bytes;
+        sm100::tma_load_2d(dst, &tm_w, fb, kt * BK, n * BM);
+        sm100::tma_load_2d(dst + p.a_bytes, &tm_a, fb, kt * BK, 0);
+        if (++kt == p.k_tiles) {
+          kt = 0;
+          ++n;
+        }
+      }
+      drain_fills(bars, p, it);
+    }
+  } else if (warp == 1) {
+    const uint32_t leader = sm100::elect_one();
+    Ring r;
+    bool ok = true;
+    int seg = 0;
+    for (int64_t u = u0; u < u1 && ok; ++seg) {
+      const int n = (int)(u / p.k_tiles);
+      const int64_t seg_end = min(u1, (int64_t)(n + 1) * p.k_tiles);
+      const int b = seg & 1;
+      if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_empty[b]), ((seg >> 1) & 1) ^ 1)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      ok = mma_stages<MN>(bars, base, p, tmem + b * kCols, (int)(seg_end - u), r, leader);
+      sm100::tc_commit(sm100::smem_u32(&bars.acc_full[b]), leader);
+      u = seg_end;
+    }
+    if (!ok && leader) set_abort(bars, kDevErrTimeoutFull);
+    sm100::tc_commit(sm100::smem_u32(bars.mma_done), leader);
+    if (!sm100::mbar_wait_warp(sm100::smem_u32(bars.mma_done), 0) && leader) b200_dev_error(kDevErrTimeoutMma);
+  } else {
+    const int quarter = warp & 3;
+    int seg = 0;
+    for (int64_t u = u0; u < u1; ++seg) {
+      const int n_tile = (int)(u / p.k_tiles);
+      const int64_t seg_end = min(u1, (int64_t)(n_tile + 1) * p.k_tiles);
+      const int count = (int)(seg_end - u);
+      u = seg_end;
+      const int b = seg & 1;
+      const bool ok = sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_full[b]), (seg >> 1) & 1);
+      if (!ok) {
+        set_abort(bars, kDevErrTimeoutMma);
+        break;
+      }
+      sm100::tc_fence_after();
+      uint32_t acc[MN];
+#pragma unroll
+      for (int c = 0; c < MN; c += 16)
+        sm100::tmem_ld_32x32b_x16(tmem + b * kCols + ((uint32_t)(quarter * 32) << 16) + c, acc + c);
+#pragma unroll
+      for (int c = 0; c < MN; c += 16) sm100::tmem_wait_ld_regs16(acc + c);
+      // the buffer is in registers: hand it back to the MMA warp
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&bars.acc_empty[b]));
+      const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
+      const bool n_ok = n < p.N && !aborted(bars);
+      if (count == p.k_tiles) {
+        if (n_ok) {
+          const float sw = sW[n];
+#pragma unroll
+          for (int m = 0; m < MN; ++m) {
+            if (m < p.M) {
+              C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant(acc[m], sA[m], sw));
+              if (acc_out) acc_out[(int64_t)m * p.N + n] = (int32_t)acc[m];
+            }
+          }
+        }
+      } else {
+        // exact int32 partial: red.add, count k tiles on the ticket, the
+        // CTA completing the count finishes the tile
+        if (n_ok) {
+#pragma unroll
+          for (int m = 0; m < MN; ++m)
+            if (m < p.M) atomicAdd(&ws[(int64_t)m * p.N + n], (int)acc[m]);
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (threadIdx.x == 2 * 32) {
+          const int prev = atomicAdd(&tickets[n_tile], count);
+          const int last = (prev + count == p.k_tiles);
+          if (last) atomicExch(&tickets[n_tile], 0);
+          bars.flags[1] = last;
+        }
+        named_bar_sync(1, 128);
+        const bool last = bars.flags[1] != 0;
+        named_bar_sync(1, 128);  // flags[1] is rewritten by the next segment
+        if (last) {
+          __threadfence();
+          if (n_ok) {
+            const float sw = sW[n];
+#pragma unroll
+            for (int m = 0; m < MN; ++m) {
+              if (m < p.M) {
+                int32_t* cell = &ws[(int64_t)m * p.N + n];
+                const int32_t v = __ldcg(cell);
+                *cell = 0;  // ready for the next call
+                C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant((uint32_t)v, sA[m], sw));
+                if (acc_out) acc_out[(int64_t)m * p.N + n] = v;
+              }
+            }
+          }
+        }
+      }
+    }
+    sm100::tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 2 * kCols);
+  }
+}
+
+// ----------------------------------------------------------------------------
 // Skinny kernel (M <= 64): C^T tiles [128 n x MN m], split-K
 // ----------------------------------------------------------------------------
 template <int MN, typename OutT>
@@ -596,6 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 struct GemmPlan {
   bool skinny;
+  bool stream;     // streaming skinny kernel (one W range per SM)
   bool pair;       // two-SM kernel (256 x 256 tiles per CTA pair)
   int b_box_rows;  // rows of the second operand's TMA box
   int BN;  // persistent tile width, or MN (padded M) for skinny
@@ -608,12 +775,17 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
   GemmPlan g{};
   g.k_tiles = (int)((K + BK - 1) / BK);
   const int sms = device_sm_count();
-  const size_t budget = 227 * 1024 - 1024 - 256;
+  // dynamic shared memory: stages, then the barrier block of carve() (full
+  // and empty per stage, 2 + 2 accumulator barriers, mma_done, the TMEM slot
+  // and two flags), plus 1 KB of alignment slack
+  auto bar_bytes = [](int st) -> size_t { return (size_t)(2 * st + 5) * 8 + 16; };
+  const size_t limit = 227 * 1024 - 1024;
   g.skinny = M <= 64 && !(cfg && (cfg->flags & 1));  // flags bit 0: force the persistent kernel
   if (g.skinny) {
     g.BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     g.m_tiles = 1;
     g.n_tiles = (int)((N + BM - 1) / BM);
+    g.stream = !(cfg && (cfg->flags & 4));  // flags bit 2: split-grid kernel instead of the streaming one
     int splits = (cfg && cfg->split > 0) ? cfg->split : 0;
     if (splits == 0) {
       splits = 1;
@@ -626,6 +798,11 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
     g.stage_bytes = g.a_bytes + g.BN * BK;
     g.grid = g.n_tiles * g.splits;
     if (g.splits > 1) g.ws_bytes = kTicketBytes + (size_t)M * N * 4;
+    if (g.stream) {
+      const int64_t units = (int64_t)g.n_tiles * g.k_tiles;
+      g.grid = (int)(units < sms ? units : sms);
+      g.ws_bytes = kTicketBytes + (size_t)M * N * 4;
+    }
   } else if (M > 128 && !(cfg && (cfg->flags & 2)) && sms >= 2) {  // flags bit 1: one-SM persistent kernel
     g.pair = true;
     g.BN = kPairN;
@@ -653,10 +830,10 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
     g.grid = (int)(tiles < sms ? tiles : sms);
   }
   g.b_box_rows = g.skinny ? g.BN : (g.pair ? kPairN / 2 : g.BN);
-  int stages = (cfg && cfg->stages > 0) ? cfg->stages : 8;
-  while (stages > 2 && (size_t)stages * g.stage_bytes > budget) --stages;
+  int stages = (cfg && cfg->stages > 0) ? cfg->stages : (g.stream ? 16 : 8);
+  while (stages > 2 && (size_t)stages * g.stage_bytes + bar_bytes(stages) > limit) --stages;
   g.stages = stages;
-  g.smem = (size_t)stages * g.stage_bytes + 1024 + 256;
+  g.smem = (size_t)stages * g.stage_bytes + bar_bytes(stages) + 1024;
   return g;
 }
 
@@ -688,6 +865,16 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
     if (e != cudaSuccess) return launch_status(e);
     kern<<<g.grid, kThreads, g.smem, s>>>(ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, p);
+    return launch_status(cudaGetLastError());
+  }
+  if (g.stream) {
+    auto kern = g.BN == 16 ? int8_gemm_stream_kernel<16, OutT>
+                           : (g.BN == 32 ? int8_gemm_stream_kernel<32, OutT> : int8_gemm_stream_kernel<64, OutT>);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+    if (e != cudaSuccess) return launch_status(e);
+    int* tickets = static_cast<int*>(ws);
+    int32_t* part = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + kTicketBytes);
+    kern<<<g.grid, kThreads, g.smem, s>>>(ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, part, tickets, p);
     return launch_status(cudaGetLastError());
   }
   auto sk = g.BN == 16 ? int8_gemm_skinny_kernel<16, OutT>
@@ -729,7 +916,7 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
   if (!aligned16(A) || !aligned16(W)) return B200_ERR_ALIGNMENT;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
   const GemmPlan g = plan_gemm(M, N, K, cfg);
-  if (g.skinny && g.splits > 1) {
+  if (g.skinny && (g.splits > 1 || g.stream)) {
     if (workspace == nullptr || workspace_bytes < g.ws_bytes || !aligned16(workspace)) return B200_ERR_WORKSPACE;
     if ((size_t)g.n_tiles * 4 > kTicketBytes) return B200_ERR_UNSUPPORTED;
   }
