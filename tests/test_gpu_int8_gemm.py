@@ -48,7 +48,8 @@ def test_int8_gemm_configs(cfg, cuda_device):
 # small M: the streaming kernel (default; W cut into one k-range per SM) and
 # the split-grid kernel (flags bit 2), with ragged N and K and repeated calls
 # (the partial-sum workspace must come back to zero)
-@pytest.mark.parametrize("cfg", [None, {"flags": 4}, {"stages": 3}, {"flags": 4, "split": 3}])
+@pytest.mark.parametrize("cfg", [None, {"flags": 4}, {"stages": 3}, {"flags": 4, "split": 3}, {"tile_k": 128},
+                                 {"tile_k": 1024, "stages": 2}])
 @pytest.mark.parametrize("M,N,K_", [(1, 300, 4096), (16, 1000, 1008), (33, 4096, 640), (64, 2000, 8192)])
 def test_int8_gemm_skinny_kernels(cfg, M, N, K_, cuda_device):
     for seed in (0, 1):

@@ -37,6 +37,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage
+static_assert(BK / 32 == 4, "four K=32 MMA steps per k tile");
 constexpr int kThreads = 192;
 // Split-K tickets live in a fixed region at the start of the workspace so
 // that calls of different shapes sharing one buffer find them at zero.
@@ -50,7 +51,9 @@ struct GemmParams {
   int stages;
   int m_tiles, n_tiles, num_tiles;
   uint32_t stage_bytes;
-  uint32_t a_bytes;     // bytes of the first operand box in a stage
+  uint32_t a_bytes;     // bytes of the first operand box(es) in a stage
+  int group;            // streaming kernel: k tiles per stage
+  int k_groups;         // streaming kernel: ceil(k_tiles / group)
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -503,8 +506,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Bars bars = carve(smem, p);
   const uint32_t base = sm100::smem_u32(smem);
-  constexpr int kCols = MN < 32 ? 32 : MN;  // TMEM allocation granularity, per buffer
-  const int64_t U = (int64_t)p.n_tiles * p.k_tiles;
+  // kChains accumulators per buffer: consecutive MMAs of a segment rotate
+  // over them, so the MMA pipe runs kChains independent accumulation chains
+  // instead of one (an M=128, N<=64 MMA is far shorter than its latency);
+  // the epilogue sums them (exact int32).
+  constexpr int kChains = 4;
+  constexpr int kChainCols = MN < 32 ? 32 : MN;   // chains start on 32-column boundaries
+  constexpr int kCols = kChains * kChainCols;     // TMEM columns per buffer (a power of two >= 128)
+  // work units: (n tile, group of p.group k tiles), n-major
+  const int64_t U = (int64_t)p.n_tiles * p.k_groups;
   const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
   if (threadIdx.x == 0) init_bars(bars, p);
   if (warp == 1) {
@@ -515,8 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *bars.tmem_slot;
-  const int n_first = (int)(u0 / p.k_tiles);
-  const int kt_first = (int)(u0 - (int64_t)n_first * p.k_tiles);
+  const int n_first = (int)(u0 / p.k_groups);
+  const int kg_first = (int)(u0 - (int64_t)n_first * p.k_groups);
+  const uint32_t w_box = BM * BK, a_box = MN * BK;  // bytes of one k tile of W / of A
 
   if (warp == 0) {
     if (lane == 0) {
@@ -524,19 +535,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tma_prefetch_desc(&tm_a);
       int it = 0;
       Ring r;
-      int n = n_first, kt = kt_first;
+      int n = n_first, kg = kg_first;
       for (int64_t u = u0; u < u1; ++u, ++it, r.next(p.stages)) {
         if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[r.s]), r.ph ^ 1u) || aborted(bars)) {
           set_abort(bars, kDevErrTimeoutEmpty);
           break;
         }
         const uint32_t fb = sm100::smem_u32(&bars.full[r.s]);
-        sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
+        sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);  // boxes past K arrive zero-filled, full size
         const uint32_t dst = base + r.s * p.stage_bytes;
-        sm100::tma_load_2d(dst, &tm_w, fb, kt * BK, n * BM);
-        sm100::tma_load_2d(dst + p.a_bytes, &tm_a, fb, kt * BK, 0);
-        if (++kt == p.k_tiles) {
-          kt = 0;
+        // the group's W boxes back to back: each W row is read as one run of
+        // group * 128 contiguous bytes
+        for (int g = 0; g < p.group; ++g)
+          sm100::tma_load_2d(dst + g * w_box, &tm_w, fb, (kg * p.group + g) * BK, n * BM);
+        for (int g = 0; g < p.group; ++g)
+          sm100::tma_load_2d(dst + p.a_bytes + g * a_box, &tm_a, fb, (kg * p.group + g) * BK, 0);
+        if (++kg == p.k_groups) {
+          kg = 0;
           ++n;
         }
       }
@@ -547,16 +562,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     Ring r;
     bool ok = true;
     int seg = 0;
+    constexpr uint32_t idesc = sm100::make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, 0, 0, BM, MN);
+    const uint64_t wd0 = sm100::make_smem_desc(base, 16, 1024, sm100::kSwizzle128B);
+    const uint64_t ad0 = sm100::make_smem_desc(base + p.a_bytes, 16, 1024, sm100::kSwizzle128B);
     for (int64_t u = u0; u < u1 && ok; ++seg) {
-      const int n = (int)(u / p.k_tiles);
-      const int64_t seg_end = min(u1, (int64_t)(n + 1) * p.k_tiles);
+      const int n = (int)(u / p.k_groups);
+      const int64_t seg_end = min(u1, (int64_t)(n + 1) * p.k_groups);
       const int b = seg & 1;
       if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_empty[b]), ((seg >> 1) & 1) ^ 1)) {
         ok = false;
         break;
       }
       sm100::tc_fence_after();
-      ok = mma_stages<MN>(bars, base, p, tmem + b * kCols, (int)(seg_end - u), r, leader);
+      const uint32_t d_buf = tmem + b * kCols;
+      for (int64_t i = 0; u + i < seg_end && ok; ++i, r.next(p.stages)) {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.full[r.s]), r.ph) || aborted(bars)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint64_t so = (uint64_t)((r.s * p.stage_bytes) >> 4);
+        for (int g = 0; g < p.group; ++g) {
+          const uint64_t wg = wd0 + so + (uint64_t)((g * w_box) >> 4), ag = ad0 + so + (uint64_t)((g * a_box) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            // chain kk (BK / 32 == kChains); its first MMA in the segment overwrites
+            sm100::mma_i8_ss(d_buf + kk * kChainCols, wg + 2 * kk, ag + 2 * kk, idesc, (i > 0 || g > 0) ? 1u : 0u,
+                             leader);
+          }
+        }
+        sm100::tc_commit(sm100::smem_u32(&bars.empty[r.s]), leader);
+      }
       sm100::tc_commit(sm100::smem_u32(&bars.acc_full[b]), leader);
       u = seg_end;
     }
@@ -567,8 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     int seg = 0;
     for (int64_t u = u0; u < u1; ++seg) {
-      const int n_tile = (int)(u / p.k_tiles);
-      const int64_t seg_end = min(u1, (int64_t)(n_tile + 1) * p.k_tiles);
+      const int n_tile = (int)(u / p.k_groups);
+      const int64_t seg_end = min(u1, (int64_t)(n_tile + 1) * p.k_groups);
       const int count = (int)(seg_end - u);
       u = seg_end;
       const int b = seg & 1;
@@ -580,17 +616,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tc_fence_after();
       uint32_t acc[MN];
 #pragma unroll
-      for (int c = 0; c < MN; c += 16)
-        sm100::tmem_ld_32x32b_x16(tmem + b * kCols + ((uint32_t)(quarter * 32) << 16) + c, acc + c);
+      for (int j = 0; j < MN; ++j) acc[j] = 0;
 #pragma unroll
-      for (int c = 0; c < MN; c += 16) sm100::tmem_wait_ld_regs16(acc + c);
+      for (int ch = 0; ch < kChains; ++ch) {
+        uint32_t part[MN];
+#pragma unroll
+        for (int c = 0; c < MN; c += 16)
+          sm100::tmem_ld_32x32b_x16(tmem + b * kCols + ch * kChainCols + ((uint32_t)(quarter * 32) << 16) + c,
+                                    part + c);
+#pragma unroll
+        for (int c = 0; c < MN; c += 16) sm100::tmem_wait_ld_regs16(part + c);
+#pragma unroll
+        for (int j = 0; j < MN; ++j) acc[j] += part[j];
+      }
       // the buffer is in registers: hand it back to the MMA warp
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&bars.acc_empty[b]));
       const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
       const bool n_ok = n < p.N && !aborted(bars);
-      if (count == p.k_tiles) {
+      if (count == p.k_groups) {
         if (n_ok) {
           const float sw = sW[n];
 #pragma unroll
@@ -613,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(1, 128);
         if (threadIdx.x == 2 * 32) {
           const int prev = atomicAdd(&tickets[n_tile], count);
-          const int last = (prev + count == p.k_tiles);
+          const int last = (prev + count == p.k_groups);
           if (last) atomicExch(&tickets[n_tile], 0);
           bars.flags[1] = last;
         }
@@ -763,6 +808,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 struct GemmPlan {
   bool skinny;
   bool stream;     // streaming skinny kernel (one W range per SM)
+  int group, k_groups;  // streaming kernel: k tiles per stage, groups per n tile
   bool pair;       // two-SM kernel (256 x 256 tiles per CTA pair)
   int b_box_rows;  // rows of the second operand's TMA box
   int BN;  // persistent tile width, or MN (padded M) for skinny
@@ -799,7 +845,17 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
     g.grid = g.n_tiles * g.splits;
     if (g.splits > 1) g.ws_bytes = kTicketBytes + (size_t)M * N * 4;
     if (g.stream) {
-      const int64_t units = (int64_t)g.n_tiles * g.k_tiles;
+      // k tiles per stage: tile_k (bytes of K) / 128, default 4 (2 for M > 32)
+      int grp = (cfg && cfg->tile_k > 0) ? cfg->tile_k / BK : (g.BN > 32 ? 2 : 4);
+      grp = grp < 1 ? 1 : (grp > 8 ? 8 : grp);
+      if (grp > g.k_tiles) grp = g.k_tiles;
+      // at least two stages must fit in shared memory
+      while (grp > 1 && 2 * (size_t)grp * (BM + g.BN) * BK + bar_bytes(2) > limit) --grp;
+      g.group = grp;
+      g.k_groups = (g.k_tiles + grp - 1) / grp;
+      g.a_bytes = (uint32_t)grp * BM * BK;
+      g.stage_bytes = (uint32_t)grp * (BM + g.BN) * BK;
+      const int64_t units = (int64_t)g.n_tiles * g.k_groups;
       g.grid = (int)(units < sms ? units : sms);
       g.ws_bytes = kTicketBytes + (size_t)M * N * 4;
     }
@@ -957,6 +1013,8 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
   p.num_tiles = g.m_tiles * g.n_tiles;
   p.stage_bytes = g.stage_bytes;
   p.a_bytes = g.a_bytes;
+  p.group = g.group;
+  p.k_groups = g.k_groups;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (out_dtype) {
     case B200_F16: return launch<__half>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
