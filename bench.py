@@ -192,12 +192,15 @@ def secondary_ops(dev) -> dict:
 
 
 def sharded_gemm(dev, dist, ws) -> dict:
-    """quant_matmul split by output columns over the ranks: each rank runs the
-    tcgen05 GEMM on its W rows, then an NCCL all-gather over NVLink and one
-    placement copy assemble the full [M, N] output on every rank.  Timed on
-    the device as the max over ranks, all-gather included."""
+    """quant_matmul split by output columns over the ranks, timed on the device
+    as the max over ranks, two ways: (1) the tcgen05 GEMM on each rank's W
+    rows, then an NCCL all-gather over NVLink and one placement copy; (2) the
+    all-gather fused into the GEMM -- each epilogue stores its tiles into every
+    rank's C over NVLink, then a one-warp flag exchange.  Roofline of (2): the
+    slower of the GEMM at the INT8 peak and the bytes each rank sends over
+    NVLink at the measured 770 GB/s per direction."""
     from b200ops import workloads as WL
-    from b200ops.dist.collectives import sharded_int8_gemm
+    from b200ops.dist.collectives import FusedAllGatherGemm, sharded_int8_gemm
     from b200ops.dist.sharding import column_shard
     from b200ops.runtime import ops as K
 
@@ -210,22 +213,36 @@ def sharded_gemm(dev, dist, ws) -> dict:
     def gemm(A_, W_, sA_, sW_, out):
         K.int8_gemm(A_, W_, sA_, sW_, out=out)
 
-    fn = lambda: sharded_int8_gemm(A, Wl, sA, sWl, N, gemm)  # noqa: E731
-    for _ in range(3):
-        fn()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 10
-    e0.record()
-    for _ in range(reps):
-        fn()
-    e1.record()
-    torch.cuda.synchronize()
-    us = max_over_ranks(dist, e0.elapsed_time(e1) * 1e3 / reps, dev)
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(dist, e0.elapsed_time(e1) * 1e3 / reps, dev)
+
     ops = 2 * M * N * Kd
-    return {f"int8_gemm_colsharded_M{M}_N{N}_K{Kd}_x{ws}": {"us": us, "TOPS_total": ops / us / 1e6,
-                                                           "includes": "local GEMM + NCCL all-gather + placement"}}
+    us_nccl = timed(lambda: sharded_int8_gemm(A, Wl, sA, sWl, N, gemm))
+    fused = FusedAllGatherGemm(M, N, device=dev)
+    us_fused = timed(lambda: fused(A, Wl, sA, sWl))
+    fused.close()
+    peaks = measured_peaks()
+    link_gbs = 770.0
+    sent = (ws - 1) * M * (n1 - n0) * 2
+    target_us = max(ops / ws / (2 * peaks["bf16_tflops"]) / 1e6, sent / link_gbs / 1e3)
+    return {
+        f"int8_gemm_colsharded_M{M}_N{N}_K{Kd}_x{ws}": {
+            "us": us_nccl, "TOPS_total": ops / us_nccl / 1e6, "includes": "local GEMM + NCCL all-gather + placement"},
+        f"int8_gemm_allgather_fused_M{M}_N{N}_K{Kd}_x{ws}": {
+            "us": us_fused, "TOPS_total": ops / us_fused / 1e6, "nvlink_bytes_sent_per_rank": sent,
+            "roofline_us": target_us, "frac": target_us / us_fused,
+            "includes": "GEMM with peer-store epilogue + flag exchange"},
+    }
 
 
 # --------------------------------------------------------------------------- B200

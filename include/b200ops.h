@@ -214,6 +214,41 @@ int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
                    void* workspace, size_t workspace_bytes,
                    const b200_launch_cfg* cfg, void* stream);
 
+/* ---- column-sharded INT8 GEMM with the all-gather fused (multi-GPU) --------
+ * No counterpart in the reference (which runs on one device): the
+ * multi-GPU layout of quant_matmul partitions W by output columns, and
+ * instead of a GEMM followed by an all-gather, each rank's epilogue stores
+ * every dequantised output tile straight into the C buffer of every rank
+ * over NVLink (peer stores; no collective library call).
+ *
+ * This rank computes C[:, col0 : col0 + n_local] = dequant(A W_local^T)
+ * (the b200_int8_gemm formula) and writes it into C_ranks[r] for every rank
+ * r < world (device pointers valid on this device: peers' buffers opened
+ * with b200_ipc_open, this rank's own at index `rank`; all with the same
+ * ldc).  It then stores `epoch` into sig_ranks[r][rank] for every r and
+ * waits -- bounded, B200_ERR_DEVICE_TIMEOUT in the device error word on
+ * expiry -- until sig_ranks[rank][r] >= epoch for every r, i.e. until every
+ * rank's columns have landed in this rank's C.  sig arrays: `world` uint32
+ * each, zero before the first call; epoch: strictly increasing per call.
+ * All ranks must call it with the same M, K, epoch and world. */
+int b200_int8_gemm_allgather(const int8_t* A, const int8_t* W_local, const float* sA,
+                             const float* sW_local, void* const* C_ranks,
+                             uint32_t* const* sig_ranks, int32_t world, int32_t rank,
+                             int64_t M, int64_t n_local, int64_t col0, int64_t K,
+                             int64_t ldc, int32_t out_dtype, uint32_t epoch,
+                             void* workspace, size_t workspace_bytes,
+                             const b200_launch_cfg* cfg, void* stream);
+
+/* ---- CUDA IPC for peer buffers (no counterpart in the reference) -----------
+ * handle: 64 opaque bytes naming dev_ptr's whole allocation, and offset:
+ * dev_ptr's byte offset inside it (allocators hand out pieces of larger
+ * allocations).  b200_ipc_open maps another process's buffer on this device
+ * (peer access over NVLink enabled) and returns base + offset;
+ * b200_ipc_close unmaps it (same offset). */
+int b200_ipc_handle(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int b200_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out);
+int b200_ipc_close(void* dev_ptr, int64_t offset);
+
 /* ---- symmetric INT8 quantisation -------------------------------------------
  * Restates triton_agent/ops/quant_matmul/reference.py:16-24:
  *   scale = max|x| / 127 (0 -> 1e-6), q = clamp(round_half_even(x / scale), -127, 127)

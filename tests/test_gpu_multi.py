@@ -50,6 +50,24 @@ def _worker(rank, world, port, q):
         C = sharded_int8_gemm(A, W[n0:n1].contiguous(), sA, sW[n0:n1].contiguous(), N,
                               lambda a, w, s1, s2, out: K.int8_gemm(a, w, s1, s2, out=out))
         gemm_ok = bool(torch.equal(C, full))
+        # the same GEMM with the all-gather fused into the epilogue (peer
+        # stores over NVLink): bit-identical, twice (the flags' epochs advance),
+        # and for a small M (persistent one-SM kernel) on a fresh object
+        from b200ops.dist.collectives import FusedAllGatherGemm
+        fused = FusedAllGatherGemm(M, N, device=dev)
+        for _ in range(2):
+            Cf = fused(A, W[n0:n1].contiguous(), sA, sW[n0:n1].contiguous())
+            torch.cuda.synchronize()
+            gemm_ok = gemm_ok and bool(torch.equal(Cf, full))
+        fused.close()
+        A2, W2, sA2, sW2 = WL.int8_gemm_inputs(40, 1000, 256, device=dev, seed=7)
+        full2 = K.int8_gemm(A2, W2, sA2, sW2)
+        m0, m1 = column_shard(1000, world, rank)
+        fused2 = FusedAllGatherGemm(40, 1000, device=dev)
+        C2 = fused2(A2, W2[m0:m1].contiguous(), sA2, sW2[m0:m1].contiguous())
+        torch.cuda.synchronize()
+        gemm_ok = gemm_ok and bool(torch.equal(C2, full2)) and K.read_device_error(dev) == 0
+        fused2.close()
         # batch-sharded decode: same inputs on every rank, each computes its share
         cache = WL.paged_cache(num_blocks=2048, block_size=16, Hkv=8, D=128, device=dev, seed=6)
         att = WL.decode_attention_inputs(cache, B=16, Hq=32, ctx_lo=100, ctx_hi=1500, device=dev, seed=6)

@@ -11,7 +11,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 from pathlib import Path
 
 PKG_ROOT = Path(__file__).resolve().parents[2]
@@ -100,6 +100,14 @@ SIGNATURES = {
     ),
     "b200_int8_gemm_workspace_size": (c_size_t, [I64_, I64_, I64_, PCFG]),
     "b200_int8_gemm": (c_int, [P, P, P, P, P, I64_, I64_, I64_, I64_, c_int32, P, P, c_size_t, PCFG, P]),
+    "b200_int8_gemm_allgather": (
+        c_int,
+        [P, P, P, P, POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int32, I64_, I64_, I64_, I64_, I64_, c_int32,
+         c_uint32, P, c_size_t, PCFG, P],
+    ),
+    "b200_ipc_handle": (c_int, [P, P, POINTER(c_int64)]),
+    "b200_ipc_open": (c_int, [P, I64_, POINTER(c_void_p)]),
+    "b200_ipc_close": (c_int, [P, I64_]),
     "b200_quantize_int8": (c_int, [P, P, P, I64_, I64_, c_int32, c_int32, PCFG, P]),
     "b200_flash_attn": (
         c_int, [P, P, P, P, P, I64_, I64_, I64_, I64_, I64_, c_float, c_int32, c_int32, PCFG, P]

@@ -1269,68 +1269,85 @@ __global__ void __launch_bounds__(kThreads3, 1)
       for (uint32_t it = rit > kRing3 ? rit - kRing3 : 0; it < rit; ++it)
         if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[it % kRing3]), (it / kRing3) & 1))
           b200_dev_error(kDevErrTimeoutFull);
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
       // ----------------------------------------------------------- MMA issue
+      // The whole warp runs the loop (waits, descriptors and ring position
+      // stay warp-uniform); one elected lane issues the MMAs and commits.
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_s = sm100::make_idesc(1, fmt, fmt, 0, 0, kBM, kBN);
       constexpr uint32_t idesc_o = sm100::make_idesc(1, fmt, fmt, 0, 1, kBM, D);
+      const uint32_t leader = sm100::elect_one();
+      // descriptors at offset 0; slots and K steps add (bytes >> 4) to the
+      // start-address field, which never carries (addresses < 2^18)
+      const uint64_t dq0 = sm100::make_smem_desc(sbase + L::oQA, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t dq1 = sm100::make_smem_desc(sbase + L::oQB, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t dk = sm100::make_smem_desc(sbase + L::oRing, 16, 1024, sm100::kSwizzle128B);
+      const uint64_t dv = sm100::make_smem_desc(sbase + L::oRing, L::kHalf, 1024, sm100::kSwizzle128B);
       uint32_t rbase = 0;          // ring item of K_0 of the current work item
       uint32_t pc0 = 0, pc1 = 0;   // P releases consumed per tile
       bool ok = true;
-      auto ring_wait = [&](uint32_t it) -> uint32_t {
-        const uint32_t slot = it % kRing3;
-        if (!sm100::mbar_wait(sm100::smem_u32(&ring_full[slot]), (it / kRing3) & 1)) return 0u;
-        sm100::tc_fence_after();
-        return sbase + L::oRing + slot * L::kTile;
+      // ring item it (K_j = rbase + 2j, V_j = rbase + 2j + 1): slot it % kRing3,
+      // fill phase (it / kRing3) & 1, advanced two items at a time
+      auto adv2 = [](int& slot, uint32_t& ph) {
+        slot += 2;
+        if (slot >= kRing3) {
+          slot -= kRing3;
+          ph ^= 1u;
+        }
       };
-      auto release = [&](uint32_t it) { sm100::tc_commit(sm100::smem_u32(&ring_empty[it % kRing3])); };
-      auto issue_s = [&](int t, int j) -> bool {
-        const uint32_t kbase = ring_wait(rbase + 2 * j);
-        if (!kbase) return false;
-        const uint32_t qbase = sbase + (t ? L::oQB : L::oQA);
+      auto issue_s = [&](int t, int slot, uint32_t ph) -> bool {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&ring_full[slot]), ph)) return false;
+        sm100::tc_fence_after();
+        const uint64_t ad = t ? dq1 : dq0;
+        const uint64_t bd = dk + (uint64_t)((slot * L::kTile) >> 4);
+        const uint32_t d_tmem = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kHalf + (kk & 3) * 32;
-          const uint64_t ad = sm100::make_smem_desc(qbase + off, 16, 1024, sm100::kSwizzle128B);
-          const uint64_t bd = sm100::make_smem_desc(kbase + off, 16, 1024, sm100::kSwizzle128B);
-          sm100::mma_f16_ss(tmem + t * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * L::kHalf + (kk & 3) * 32) >> 4;
+          sm100::mma_f16_ss(d_tmem, ad + off, bd + off, idesc_s, kk > 0 ? 1u : 0u, leader);
         }
-        sm100::tc_commit(sm100::smem_u32(&s_full[t]));
+        sm100::tc_commit(sm100::smem_u32(&s_full[t]), leader);
         return true;
       };
-      auto issue_pv = [&](int t, int j) -> bool {
-        if (!sm100::mbar_wait(sm100::smem_u32(&p_full[t]), (t ? pc1 : pc0) & 1)) return false;
+      auto issue_pv = [&](int t, int j, int slot, uint32_t ph) -> bool {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&p_full[t]), (t ? pc1 : pc0) & 1)) return false;
         if (t) ++pc1; else ++pc0;
-        const uint32_t vbase = ring_wait(rbase + 2 * j + 1);
-        if (!vbase) return false;
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&ring_full[slot]), ph)) return false;
+        sm100::tc_fence_after();
+        const uint64_t bd = dv + (uint64_t)((slot * L::kTile) >> 4);
+        const uint32_t d_tmem = tmem + 256 + t * 128, a_tmem = tmem + t * 128;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = sm100::make_smem_desc(vbase + kk * 2048, L::kHalf, 1024, sm100::kSwizzle128B);
-          sm100::mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          sm100::mma_f16_ts(d_tmem, a_tmem + kk * 8, bd + (uint64_t)((kk * 2048) >> 4), idesc_o,
+                            (j > 0 || kk > 0) ? 1u : 0u, leader);
         return true;
       };
+      auto release = [&](int slot) { sm100::tc_commit(sm100::smem_u32(&ring_empty[slot]), leader); };
       for (int k = 0; ok; ++k) {
         const int qs = k & 1;
-        if (!sm100::mbar_wait(sm100::smem_u32(&item_full[qs]), (k >> 1) & 1)) {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&item_full[qs]), (k >> 1) & 1)) {
           ok = false;
           break;
         }
         const int id = *(volatile int*)&item_q[qs];
-        sm100::mbar_arrive(sm100::smem_u32(&item_empty[qs]));
+        __syncwarp();
+        if (leader) sm100::mbar_arrive(sm100::smem_u32(&item_empty[qs]));
         if (id < 0) break;
         int bh, ct, n0, n1;
         flash_item(p, n_ct, id, bh, ct);
         flash_kt(p, ct, n0, n1);
-        if (!sm100::mbar_wait(sm100::smem_u32(q_full), k & 1)) {
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(q_full), k & 1)) {
           ok = false;
           break;
         }
         sm100::tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) ok = issue_s(t, 0);
+        int k_slot = (int)(rbase % kRing3), v_slot = (int)((rbase + 1) % kRing3);
+        uint32_t k_ph = (rbase / kRing3) & 1, v_ph = ((rbase + 1) / kRing3) & 1;
+        for (int t = 0; t < 2 && ok; ++t) ok = issue_s(t, k_slot, k_ph);
         if (!ok) break;
-        release(rbase);  // K_0
-        if (n1 == 1) sm100::tc_commit(sm100::smem_u32(q_empty));
+        release(k_slot);  // K_0
+        adv2(k_slot, k_ph);
+        if (n1 == 1) sm100::tc_commit(sm100::smem_u32(q_empty), leader);
         for (int j = 0; ok && j < n1; ++j) {
           if (*(volatile int*)s_abort) {
             ok = false;
@@ -1340,24 +1357,26 @@ __global__ void __launch_bounds__(kThreads3, 1)
             const int nkt = t ? n1 : n0;
             if (j >= nkt) continue;
             // O_t of the previous work item must be drained before PV_t(0) overwrites it
-            if (j == 0 && k > 0 && !sm100::mbar_wait(sm100::smem_u32(&o_empty[t]), (k - 1) & 1)) {
+            if (j == 0 && k > 0 && !sm100::mbar_wait_warp(sm100::smem_u32(&o_empty[t]), (k - 1) & 1)) {
               ok = false;
               break;
             }
-            ok = issue_pv(t, j);
-            if (ok && t == 1) release(rbase + 2 * j + 1);  // V_j: tile B reads it last
+            ok = issue_pv(t, j, v_slot, v_ph);
+            if (ok && t == 1) release(v_slot);  // V_j: tile B reads it last
             if (ok && j + 1 < nkt) {
-              ok = issue_s(t, j + 1);
+              ok = issue_s(t, k_slot, k_ph);
               // the last S MMA of the item (tile B's, as n1 >= n0) frees Q
-              if (ok && t == 1 && j + 2 == n1) sm100::tc_commit(sm100::smem_u32(q_empty));
+              if (ok && t == 1 && j + 2 == n1) sm100::tc_commit(sm100::smem_u32(q_empty), leader);
             }
-            if (ok && j + 1 == nkt) sm100::tc_commit(sm100::smem_u32(&o_full[t]));
+            if (ok && j + 1 == nkt) sm100::tc_commit(sm100::smem_u32(&o_full[t]), leader);
           }
-          if (ok && j + 1 < n1) release(rbase + 2 * j + 2);  // K_{j+1}
+          if (ok && j + 1 < n1) release(k_slot);  // K_{j+1}
+          adv2(k_slot, k_ph);
+          adv2(v_slot, v_ph);
         }
         rbase += 2 * n1;
       }
-      if (!ok) {
+      if (!ok && leader) {
         b200_dev_error(kDevErrTimeoutFull);
         atomicExch(s_abort, 1);
       }

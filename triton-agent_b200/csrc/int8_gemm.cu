@@ -36,6 +36,7 @@ namespace b200 {
 namespace {
 
 constexpr int BM = 128;
+constexpr int kMaxRanks = 8;  // fused all-gather: ranks of one node
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage
 static_assert(BK / 32 == 4, "four K=32 MMA steps per k tile");
 constexpr int kThreads = 192;
@@ -54,6 +55,12 @@ struct GemmParams {
   uint32_t a_bytes;     // bytes of the first operand box(es) in a stage
   int group;            // streaming kernel: k tiles per stage
   int k_groups;         // streaming kernel: ceil(k_tiles / group)
+  // fused all-gather (world > 0): every output chunk also goes to dst[r]
+  // (C of rank r, this device's view) at column offset col_off; rank `self`'s
+  // own copy is the kernel's C argument
+  int world, self;
+  int64_t col_off;
+  void* dst[kMaxRanks];
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -99,8 +106,17 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row,
     const float sw = (j < n_valid) ? __ldg(&sW[col0 + j]) : 0.f;
     v[j] = dequant(acc[j], sa, sw);
   }
-  OutT* dst = C + row * p.ldc + col0;
-  store_out_row<OutT>(dst, v, n_valid, (reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+  const int64_t off = row * p.ldc + col0 + p.col_off;
+  OutT* dst = C + off;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+  store_out_row<OutT>(dst, v, n_valid, vec_ok);
+  // fused all-gather: the same chunk into every peer's C over NVLink, in an
+  // order rotated by rank so the ranks' stores spread over all links
+  for (int i = 1; i < p.world; ++i) {
+    int r = p.self + i;
+    if (r >= p.world) r -= p.world;
+    store_out_row<OutT>(static_cast<OutT*>(p.dst[r]) + off, v, n_valid, vec_ok);
+  }
   if (acc_out != nullptr) {
     int32_t* ad = acc_out + row * p.N + col0;
     if (n_valid == 32 && ((reinterpret_cast<uintptr_t>(ad) & 15u) == 0)) {
@@ -115,6 +131,54 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row,
   }
 }
 
+// Fused all-gather epilogue for 128 columns of a warp's 32 accumulator rows
+// (16-bit outputs): dequantise in registers, stage [32 rows][128 cols] in
+// the warp's shared buffer, then write it back row by row -- 16 lanes x 16 B,
+// one 256-byte run per row -- into this rank's C and every peer's C.  A warp
+// writing 32 rows x 16 B per instruction would reach the peers as 16-byte
+// NVLink writes; whole rows go as 256-byte runs.
+constexpr int kGatherCols = 128;
+constexpr int kGatherRowBytes = kGatherCols * 2 + 16;  // +16 B: conflict-free both ways
+constexpr int kGatherWarpBytes = 32 * kGatherRowBytes;
+
+template <typename OutT>
+__device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int lane, int64_t col0,
+                                             const float* __restrict__ sA, const float* __restrict__ sW,
+                                             OutT* __restrict__ C, const GemmParams& p, uint8_t* stage) {
+  static_assert(sizeof(OutT) == 2, "staged gather is for 16-bit outputs");
+  const int64_t row = row0 + lane;
+  const float sa = row < p.M ? sA[row] : 0.f;
+#pragma unroll 1
+  for (int c4 = 0; c4 < kGatherCols / 32; ++c4) {
+    uint32_t acc[32];
+    sm100::tmem_ld_32x32b_x32(t_row + c4 * 32, acc);
+    sm100::tmem_wait_ld_regs(acc);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = dequant(acc[j], sa, __ldg(&sW[col0 + c4 * 32 + j]));
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(stage + lane * kGatherRowBytes + c4 * 64 + q * 16) = pack16<OutT>(v + 8 * q);
+  }
+  __syncwarp();
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int r = 2 * i + (lane >> 4), piece = lane & 15;
+    const uint4 w = *reinterpret_cast<const uint4*>(stage + r * kGatherRowBytes + piece * 16);
+    const int64_t grow = row0 + r;
+    if (grow < p.M) {
+      const int64_t off = grow * p.ldc + p.col_off + col0 + piece * 8;
+      *reinterpret_cast<uint4*>(C + off) = w;
+      for (int k = 1; k < p.world; ++k) {
+        int d = p.self + k;
+        if (d >= p.world) d -= p.world;
+        *reinterpret_cast<uint4*>(static_cast<OutT*>(p.dst[d]) + off) = w;
+      }
+    }
+  }
+  __syncwarp();
+}
+
 // Shared-memory carve-up of both kernels: [ring of stages][barriers...]
 struct Bars {
   uint64_t* full;
@@ -123,7 +187,8 @@ struct Bars {
   uint64_t* acc_empty;  // [2]
   uint64_t* mma_done;
   uint32_t* tmem_slot;
-  int* flags;  // [0] abort, [1] last split
+  int* flags;      // [0] abort, [1] last split
+  uint8_t* gather;  // fused all-gather staging, kGatherWarpBytes per epilogue warp
 };
 
 __device__ __forceinline__ Bars carve(uint8_t* smem, const GemmParams& p) {
@@ -135,6 +200,7 @@ __device__ __forceinline__ Bars carve(uint8_t* smem, const GemmParams& p) {
   b.mma_done = b.acc_empty + 2;
   b.tmem_slot = reinterpret_cast<uint32_t*>(b.mma_done + 1);
   b.flags = reinterpret_cast<int*>(b.tmem_slot + 1);
+  b.gather = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(b.flags + 2) + 15) & ~uintptr_t(15));
   return b;
 }
 
@@ -301,17 +367,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (int64_t)m_tile * BM + quarter * 32 + lane;
       const uint32_t t_row = tmem + a * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < BN;) {
+        const int64_t col0 = (int64_t)n_tile * BN + c;
+        if constexpr (sizeof(OutT) == 2) {
+          if (p.world > 1 && col0 + kGatherCols <= p.N && c + kGatherCols <= BN) {  // warp-uniform
+            gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
+                               bars.gather + (warp - 2) * kGatherWarpBytes);
+            c += kGatherCols;
+            continue;
+          }
+        }
         uint32_t acc[32];
         sm100::tmem_ld_32x32b_x32(t_row + c, acc);
         sm100::tmem_wait_ld_regs(acc);
-        if (row < p.M && !aborted(bars))
-          epilogue_chunk<OutT>(acc, row, (int64_t)n_tile * BN + c, sA, sW, C, acc_out, p);
+        if (row < p.M && !aborted(bars)) epilogue_chunk<OutT>(acc, row, col0, sA, sW, C, acc_out, p);
+        c += 32;
       }
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&bars.acc_empty[a]));
     }
+    // fused all-gather: peer stores visible system-wide before the signal kernel
+    if (p.world > 1) __threadfence_system();
   }
   __syncthreads();
   if (warp == 1) {
@@ -463,17 +540,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (int64_t)m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
       const uint32_t t_row = tmem + a * kPairN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kPairN; c += 32) {
+      for (int c = 0; c < kPairN;) {
+        const int64_t col0 = (int64_t)n_tile * kPairN + c;
+        if constexpr (sizeof(OutT) == 2) {
+          if (p.world > 1 && col0 + kGatherCols <= p.N) {  // warp-uniform
+            gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
+                               bars.gather + (warp - 2) * kGatherWarpBytes);
+            c += kGatherCols;
+            continue;
+          }
+        }
         uint32_t acc[32];
         sm100::tmem_ld_32x32b_x32(t_row + c, acc);
         sm100::tmem_wait_ld_regs(acc);
-        if (row < p.M && !aborted(bars))
-          epilogue_chunk<OutT>(acc, row, (int64_t)n_tile * kPairN + c, sA, sW, C, acc_out, p);
+        if (row < p.M && !aborted(bars)) epilogue_chunk<OutT>(acc, row, col0, sA, sW, C, acc_out, p);
+        c += 32;
       }
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive_cluster(acc_empty0 + a * 8);
     }
+    // fused all-gather: peer stores visible system-wide before the signal kernel
+    if (p.world > 1) __threadfence_system();
   }
   __syncthreads();
   // neither CTA leaves (or frees TMEM) while its peer may still signal it
@@ -817,7 +905,7 @@ struct GemmPlan {
   size_t smem, ws_bytes;
 };
 
-GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) {
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, size_t extra_smem = 0) {
   GemmPlan g{};
   g.k_tiles = (int)((K + BK - 1) / BK);
   const int sms = device_sm_count();
@@ -825,7 +913,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
   // and empty per stage, 2 + 2 accumulator barriers, mma_done, the TMEM slot
   // and two flags), plus 1 KB of alignment slack
   auto bar_bytes = [](int st) -> size_t { return (size_t)(2 * st + 5) * 8 + 16; };
-  const size_t limit = 227 * 1024 - 1024;
+  const size_t limit = 227 * 1024 - 1024 - extra_smem;
   g.skinny = M <= 64 && !(cfg && (cfg->flags & 1));  // flags bit 0: force the persistent kernel
   if (g.skinny) {
     g.BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
@@ -889,7 +977,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg) 
   int stages = (cfg && cfg->stages > 0) ? cfg->stages : (g.stream ? 16 : 8);
   while (stages > 2 && (size_t)stages * g.stage_bytes + bar_bytes(stages) > limit) --stages;
   g.stages = stages;
-  g.smem = (size_t)stages * g.stage_bytes + bar_bytes(stages) + 1024;
+  g.smem = (size_t)stages * g.stage_bytes + bar_bytes(stages) + 1024 + extra_smem;
   return g;
 }
 
@@ -958,11 +1046,19 @@ extern "C" size_t b200_int8_gemm_workspace_size(int64_t M, int64_t N, int64_t K,
   return plan_gemm(M, N, K, cfg).ws_bytes;
 }
 
-extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA, const float* sW, void* C,
-                              int64_t M, int64_t N, int64_t K, int64_t ldc, int32_t out_dtype,
-                              int32_t* acc_out, void* workspace, size_t workspace_bytes,
-                              const b200_launch_cfg* cfg, void* stream) {
-  if (int e = injected_error("int8_gemm")) return e;
+namespace b200 {
+namespace {
+
+// Destinations of a fused all-gather (world 0: a plain GEMM).
+struct Gather {
+  int world = 0, self = 0;
+  int64_t col_off = 0;
+  void* dst[kMaxRanks] = {};
+};
+
+int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* sW, void* C, int64_t M, int64_t N,
+               int64_t K, int64_t ldc, int32_t out_dtype, int32_t* acc_out, void* workspace, size_t workspace_bytes,
+               const b200_launch_cfg* cfg, void* stream, const Gather& ga) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_BAD_ARG;
   if (M == 0 || N == 0) return B200_OK;
   if (!A || !W || !sA || !sW || !C) return B200_ERR_BAD_ARG;
@@ -971,7 +1067,8 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
   if (ldc < N) return B200_ERR_BAD_ARG;
   if (!aligned16(A) || !aligned16(W)) return B200_ERR_ALIGNMENT;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
-  const GemmPlan g = plan_gemm(M, N, K, cfg);
+  // fused all-gather: 16 B alignment slack + one staging buffer per epilogue warp
+  const GemmPlan g = plan_gemm(M, N, K, cfg, ga.world > 1 ? 16 + 4 * kGatherWarpBytes : 0);
   if (g.skinny && (g.splits > 1 || g.stream)) {
     if (workspace == nullptr || workspace_bytes < g.ws_bytes || !aligned16(workspace)) return B200_ERR_WORKSPACE;
     if ((size_t)g.n_tiles * 4 > kTicketBytes) return B200_ERR_UNSUPPORTED;
@@ -999,7 +1096,11 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
-  GemmParams p;
+  GemmParams p{};
+  p.world = ga.world;
+  p.self = ga.self;
+  p.col_off = ga.col_off;
+  for (int r = 0; r < kMaxRanks; ++r) p.dst[r] = ga.dst[r];
   p.M = M;
   p.N = N;
   p.K = K;
@@ -1023,3 +1124,70 @@ extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
     default: return B200_ERR_UNSUPPORTED;
   }
 }
+
+// After a fused all-gather GEMM on the same stream: thread r tells rank r
+// that this rank's columns are in r's C (release store at system scope),
+// then waits (bounded) for rank r's flag in this rank's array.
+__global__ void __launch_bounds__(32) peer_signal_wait_kernel(Gather flags, int world, int self, uint32_t epoch) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  uint32_t* mine = static_cast<uint32_t*>(flags.dst[self]);
+  uint32_t* theirs = static_cast<uint32_t*>(flags.dst[r]);
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(theirs + self), "r"(epoch) : "memory");
+  const uint64_t t0 = sm100::global_timer_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
+    if ((int32_t)(v - epoch) >= 0) break;
+    if (sm100::global_timer_ns() - t0 > sm100::kWaitTimeoutNs) {
+      b200_dev_error(kDevErrTimeoutCombine);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA, const float* sW, void* C,
+                              int64_t M, int64_t N, int64_t K, int64_t ldc, int32_t out_dtype,
+                              int32_t* acc_out, void* workspace, size_t workspace_bytes,
+                              const b200_launch_cfg* cfg, void* stream) {
+  if (int e = injected_error("int8_gemm")) return e;
+  return gemm_entry(A, W, sA, sW, C, M, N, K, ldc, out_dtype, acc_out, workspace, workspace_bytes, cfg, stream,
+                    Gather{});
+}
+
+extern "C" int b200_int8_gemm_allgather(const int8_t* A, const int8_t* W_local, const float* sA,
+                                        const float* sW_local, void* const* C_ranks, uint32_t* const* sig_ranks,
+                                        int32_t world, int32_t rank, int64_t M, int64_t n_local, int64_t col0,
+                                        int64_t K, int64_t ldc, int32_t out_dtype, uint32_t epoch, void* workspace,
+                                        size_t workspace_bytes, const b200_launch_cfg* cfg, void* stream) {
+  if (int e = injected_error("int8_gemm_allgather")) return e;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || epoch == 0) return B200_ERR_BAD_ARG;
+  if (!C_ranks || !sig_ranks || col0 < 0 || n_local < 0 || col0 + n_local > ldc) return B200_ERR_BAD_ARG;
+  Gather ga, fl;
+  ga.world = world;
+  ga.self = rank;
+  ga.col_off = col0;
+  fl.world = world;
+  fl.self = rank;
+  for (int r = 0; r < world; ++r) {
+    if (!C_ranks[r] || !sig_ranks[r] || !aligned16(C_ranks[r])) return B200_ERR_BAD_ARG;
+    ga.dst[r] = C_ranks[r];
+    fl.dst[r] = sig_ranks[r];
+  }
+  // the multi-destination epilogue belongs to the tile kernels: small M
+  // runs the persistent one-SM kernel (flags bit 0) instead of the swap-AB ones
+  b200_launch_cfg c = cfg ? *cfg : b200_launch_cfg{};
+  c.flags |= 1;
+  if (M > 0 && n_local > 0) {
+    const int st = gemm_entry(A, W_local, sA, sW_local, C_ranks[rank], M, n_local, K, ldc, out_dtype, nullptr,
+                              workspace, workspace_bytes, &c, stream, ga);
+    if (st != B200_OK) return st;
+  }
+  peer_signal_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, world, rank, epoch);
+  return launch_status(cudaGetLastError());
+}
+

@@ -136,12 +136,82 @@ const char* b200_kernel_list(void) {
          "kv_scatter_kernel\n"
          "rope_kv_append_paged_kernel\n"
          "rope_kv_append_paged_fast_kernel\n"
+         "paged_decode_flat_kernel\n"
          "paged_decode_kernel\n"
+         "paged_decode_generic_kernel\n"
+         "int8_gemm_pair_kernel\n"
          "int8_gemm_tcgen05_kernel\n"
-         "int8_splitk_reduce_kernel\n"
+         "int8_gemm_stream_kernel\n"
+         "int8_gemm_skinny_kernel\n"
+         "peer_signal_wait_kernel\n"
          "quantize_rows_kernel\n"
          "quantize_cols_kernel\n"
-         "flash_fwd_tcgen05_kernel\n";
+         "flash_fwd3_tcgen05_kernel\n"
+         "flash_fwd4_persistent_kernel\n"
+         "flash_fwd2_tcgen05_kernel\n"
+         "flash_fwd_tcgen05_kernel\n"
+         "flash_generic_kernel\n";
+}
+
+// CUDA IPC handles name whole allocations; a caching allocator hands out
+// pieces of larger ones, so the handle travels with the piece's offset from
+// its allocation base (cuMemGetAddressRange through the driver entry point).
+typedef CUresult (*addr_range_fn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static addr_range_fn get_addr_range_fn() {
+  static addr_range_fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<addr_range_fn>(p);
+  });
+  return fn;
+}
+
+int b200_ipc_handle(const void* dev_ptr, void* handle_out, int64_t* offset_out) {
+  if (!dev_ptr || !handle_out || !offset_out) return B200_ERR_BAD_ARG;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  addr_range_fn range = get_addr_range_fn();
+  if (range == nullptr) return B200_ERR_NO_DEVICE;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return B200_ERR_BAD_ARG;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) {
+    b200::set_last_error_detail(cudaGetErrorString(e));
+    return B200_ERR_LAUNCH;
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = (int64_t)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return B200_OK;
+}
+
+int b200_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out) {
+  if (!handle || !dev_ptr_out || offset < 0) return B200_ERR_BAD_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    b200::set_last_error_detail(cudaGetErrorString(e));
+    return B200_ERR_LAUNCH;
+  }
+  *dev_ptr_out = static_cast<char*>(base) + offset;
+  return B200_OK;
+}
+
+int b200_ipc_close(void* dev_ptr, int64_t offset) {
+  if (!dev_ptr || offset < 0) return B200_ERR_BAD_ARG;
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset);
+  if (e != cudaSuccess) {
+    b200::set_last_error_detail(cudaGetErrorString(e));
+    return B200_ERR_LAUNCH;
+  }
+  return B200_OK;
 }
 
 int b200_read_device_error(int32_t* out, void* stream) {
