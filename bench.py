@@ -32,6 +32,15 @@ sys.path.insert(0, str(REPO / "triton-agent_b200"))
 import torch  # noqa: E402
 
 METRIC = "paged-decode tokens/s"
+# DRAM bytes (read + write) per algorithmic byte of the paged-decode kernel,
+# from one ncu capture of `bench.py --case decode` (16384-block cache, 64
+# sequences, ctx U[512,4096]; summary in profiles/paged_decode_flat_small.md):
+# 609.19 MB of DRAM traffic for the launch's algorithmic bytes.  The full
+# launch (ctx U[512,8192], 65536 blocks) is too large for a full-set capture;
+# its traffic is this ratio times its algorithmic bytes (both grow with the
+# pages read).
+DECODE_DRAM_BYTES_SMALL = 604_376_064 + 4_816_640
+DECODE_ALGO_BYTES_SMALL = 601_964_708  # printed by the same `bench.py --case decode` run
 UNIT = "tokens/s"
 N_SEQ, HQ, HKV, D, BS, NBLK = 64, 32, 8, 128, 16, 65536
 WORKLOAD = {
@@ -338,6 +347,7 @@ def run_b200(args, ws, rank, local, dist):
     peaks = measured_peaks()
     dec_bytes = WL.decode_bytes(att["context_len"], HQ, HKV, D, BS, index_bytes=4)
     achieved = dec_bytes / (decode_ms / 1e3) / 1e9
+    traffic = DECODE_DRAM_BYTES_SMALL / DECODE_ALGO_BYTES_SMALL * dec_bytes if DECODE_ALGO_BYTES_SMALL else None
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": n, "warmup": args.warmup,
         "ms_per_step": ms / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -346,7 +356,8 @@ def run_b200(args, ws, rank, local, dist):
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "peak_src": peaks["src"], "traffic": None, "algorithmic_bytes_per_launch": dec_bytes,
+                     "peak_src": peaks["src"], "traffic": traffic, "traffic_src": "ncu DRAM bytes of the small decode case, scaled by algorithmic bytes",
+                     "algorithmic_bytes_per_launch": dec_bytes,
                      "kernel_ms": decode_ms},
         "per_op_ms": {"rope_kv_append_paged": append_ms, "paged_attention": decode_ms},
         "gpu_launches": 2 * n,
@@ -355,10 +366,9 @@ def run_b200(args, ws, rank, local, dist):
 
 
 # ------------------------------------------------------------------- CPU baseline
-def cpu_decode_sample(n_seq_sample: int, seed: int = 0):
-    """Times the oracle's decode step (append rows + paged attention) on the
-    host cores for `n_seq_sample` sequences of the workload.  Returns
-    (tokens/s, seconds, sample description)."""
+def cpu_decode_inputs(n_seq_sample: int, seed: int = 0) -> dict:
+    """Host inputs of the decode step for `n_seq_sample` sequences of the
+    workload (ctx U[512,8192], random block tables, 64 new tokens' rows)."""
     import oracle.ops as O
 
     g = torch.Generator().manual_seed(seed)
@@ -374,17 +384,27 @@ def cpu_decode_sample(n_seq_sample: int, seed: int = 0):
         k = int((ctx[b] + BS - 1) // BS)
         bt[b, :k] = table[off:off + k]
         off += k
-    q = torch.randn(n_seq_sample, HQ, D, generator=g).bfloat16()
-    kn = torch.randn(n_seq_sample, HKV, D, generator=g).bfloat16()
-    vn = torch.randn(n_seq_sample, HKV, D, generator=g).bfloat16()
-    pos = torch.randint(0, 4096, (n_seq_sample,), generator=g)
     cos, sin = O.rope_cos_sin(4096, D)
-    slots = torch.randperm(nb * BS, generator=g)[:n_seq_sample]
+    return dict(n=n_seq_sample, nb=nb, ctx=ctx, kc=kc, vc=vc, bt=bt, cos=cos, sin=sin,
+                q=torch.randn(n_seq_sample, HQ, D, generator=g).bfloat16(),
+                kn=torch.randn(n_seq_sample, HKV, D, generator=g).bfloat16(),
+                vn=torch.randn(n_seq_sample, HKV, D, generator=g).bfloat16(),
+                pos=torch.randint(0, 4096, (n_seq_sample,), generator=g),
+                slots=torch.randperm(nb * BS, generator=g)[:n_seq_sample])
+
+
+def cpu_decode_time(x: dict) -> float:
+    """Seconds of the oracle's decode step (append rows + paged attention) on
+    the host cores for the inputs of cpu_decode_inputs."""
+    import oracle.ops as O
+
     t0 = time.perf_counter()
-    O.rope_kv_append_paged(q, kn, vn, pos, cos, sin, slots, nb * BS)
-    O.paged_attention(q, kc, vc, bt, ctx)
-    dt = time.perf_counter() - t0
-    return n_seq_sample / dt, dt, f"{n_seq_sample} sequences of the decode step (ctx U[512,8192]), oracle port"
+    O.rope_kv_append_paged(x["q"], x["kn"], x["vn"], x["pos"], x["cos"], x["sin"], x["slots"], x["nb"] * BS)
+    O.paged_attention(x["q"], x["kc"], x["vc"], x["bt"], x["ctx"])
+    return time.perf_counter() - t0
+
+
+CPU_SAMPLE_DESC = "decode step of {n} sequences (ctx U[512,8192]), oracle port"
 
 
 def run_reference(args, ws, rank):
@@ -392,15 +412,12 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return None
     torch.set_num_threads(os.cpu_count() or 1)
-    sample = 8
+    sample = N_SEQ  # a step is the whole decode step of the GPU arm's workload
+    x = cpu_decode_inputs(sample, seed=1)
     for _ in range(args.warmup):
-        cpu_decode_sample(sample, seed=1)
-    rates = []
-    t_total = 0.0
-    for i in range(args.steps):
-        r, dt, desc = cpu_decode_sample(sample, seed=2 + i)
-        rates.append(r)
-        t_total += dt
+        cpu_decode_time(x)
+    t_total = sum(cpu_decode_time(x) for _ in range(args.steps))
+    desc = CPU_SAMPLE_DESC.format(n=sample)
     value = sample * args.steps / t_total
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
@@ -485,10 +502,16 @@ def main():
                 res["secondary"] = sec
         if rank == 0:
             if ws == 1 and not args.no_cpu_baseline:
+                # whole decode steps (64 sequences) repeated for about 10 s of host work
                 torch.set_num_threads(os.cpu_count() or 1)
-                r, dt, desc = cpu_decode_sample(8, seed=7)
-                res["cpu_baseline"] = {"value": r, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                                       "sample": desc, "seconds": dt}
+                x = cpu_decode_inputs(N_SEQ, seed=7)
+                cpu_decode_time(x)
+                secs, i = 0.0, 0
+                while secs < 10.0 and i < 50:
+                    secs, i = secs + cpu_decode_time(x), i + 1
+                res["cpu_baseline"] = {"value": N_SEQ * i / secs, "unit": UNIT, "cores": torch.get_num_threads(),
+                                       "kind": "port", "sample": f"{i} x " + CPU_SAMPLE_DESC.format(n=N_SEQ),
+                                       "seconds": secs}
             print(json.dumps(res))
     finally:
         if dist is not None:
