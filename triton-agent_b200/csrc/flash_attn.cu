@@ -50,6 +50,7 @@ struct FlashParams {
   int out_lse;
   int poly_exp;     // unmasked exponentials partly on the FMA pipe
   int head_group;   // heads per CTA scheduling group (three-warpgroup kernel)
+  int poly_pairs;   // of every 8 exponential pairs, how many on the FMA pipe (three-warpgroup kernel)
 };
 
 template <int D>
@@ -96,6 +97,25 @@ __device__ __forceinline__ float ex2_poly(float x) {
   const float f = x - (t - 12582912.0f);
   const float p = fmaf(fmaf(fmaf(0.0545928263f, f, 0.242218109f), f, 0.693368645f), f, 1.0f);
   return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
+// Two lanes of ex2_poly with packed fp32x2 arithmetic: the clamp, the
+// rounding split x = n + f, the cubic in f, and 2^n added to the exponent
+// field (t's low bits hold n + 1.5 * 2^23, whose excess vanishes when
+// shifted left by 23 modulo 2^32).
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  float t0, t1, r0, r1, f0, f1, q0, q1;
+  sm100::ffma2_bcast(t0, t1, x0, x1, 1.0f, kMagic);
+  sm100::ffma2_bcast(r0, r1, t0, t1, 1.0f, -kMagic);
+  sm100::ffma2(f0, f1, r0, r1, -1.0f, -1.0f, x0, x1);
+  sm100::ffma2_bcast(q0, q1, f0, f1, 0.0545928263f, 0.242218109f);
+  sm100::ffma2(q0, q1, q0, q1, f0, f1, 0.693368645f, 0.693368645f);
+  sm100::ffma2(q0, q1, q0, q1, f0, f1, 1.0f, 1.0f);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
 template <typename T>
@@ -791,8 +811,7 @@ __device__ __forceinline__ float softmax_row_to_tmem(const uint32_t (&v)[kBN], f
       sm100::ffma2_bcast(x0, x1, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), sl2, neg_m);
       float p0, p1;
       if ((i & 7) < kPoly) {
-        p0 = ex2_poly(x0);
-        p1 = ex2_poly(x1);
+        ex2_poly2(x0, x1, p0, p1);
       } else {
         p0 = ex2_approx(x0);
         p1 = ex2_approx(x1);
@@ -1050,10 +1069,12 @@ __global__ void __launch_bounds__(kThreads3, 1)
       }
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
       float rs;
-      if (full_tile && p.poly_exp)
-        rs = softmax_row_to_tmem<T, 2>(v, p.sl2, neg_m, tSt);
-      else
-        rs = softmax_row_to_tmem<T, 0>(v, p.sl2, neg_m, tSt);
+      switch (full_tile ? p.poly_pairs : 0) {
+        case 1: rs = softmax_row_to_tmem<T, 1>(v, p.sl2, neg_m, tSt); break;
+        case 2: rs = softmax_row_to_tmem<T, 2>(v, p.sl2, neg_m, tSt); break;
+        case 3: rs = softmax_row_to_tmem<T, 3>(v, p.sl2, neg_m, tSt); break;
+        default: rs = softmax_row_to_tmem<T, 0>(v, p.sl2, neg_m, tSt); break;
+      }
       // O_t holds PV_t(j-1), complete because S_t(j) is: rescale it if the
       // max moved (before P_t(j) is released to the MMA)
       if (__any_sync(0xffffffffu, rescale)) {
@@ -1684,6 +1705,7 @@ extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void
   p.out_lse = lse != nullptr;
   p.poly_exp = (cfg && (cfg->flags & 2)) ? 1 : 0;  // flags bit 1
   p.head_group = (cfg && cfg->split > 0) ? cfg->split : 8;  // split: heads per scheduling group
+  p.poly_pairs = cfg ? (cfg->tile_k & 3) : 0;               // tile_k: exponential pairs (of 8) on the FMA pipe
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc = (D == 64 || D == 128) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) &&
                   B * H <= 0x7fffffffLL && p.n_qt <= 65535 && T < (1ll << 31) && S < (1ll << 31);
