@@ -159,7 +159,8 @@ def _median_us(fn, warmup=3, repeat=20, flush_l2=False):
 
 def secondary_ops(dev) -> dict:
     """The other operators of the hot path, each timed alone with CUDA events
-    on the current stream (medians of 20): INT8 GEMM (the metric's second
+    on the current stream (medians of 20; L2 written over and read back
+    before each timed call): INT8 GEMM (the metric's second
     part), causal flash prefill, rmsnorm.  INT8 peak: no measured INT8 figure
     exists for this pool, so the fraction is against 2x the measured dense
     bf16 GEMM (the tensor core's int8:bf16 rate is 2:1) and cuBLAS int8 is
@@ -197,6 +198,22 @@ def secondary_ops(dev) -> dict:
     us = _median_us(lambda: K.rmsnorm(x, w, out=y), flush_l2=True)
     nb = 2 * x.numel() * 4 + 4096 * 4
     res["rmsnorm_fp32_8x2048x4096"] = {"us": us, "GBps": nb / us / 1e3, "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    # rmsnorm fused with the INT8 activation quantiser (bf16 in, int8 codes + f32 row scales out)
+    xb, wb = x.bfloat16().reshape(-1, 4096), w.bfloat16()
+    us = _median_us(lambda: K.rmsnorm_quant_int8(xb, wb), flush_l2=True)
+    nb = xb.numel() * 2 + xb.numel() + xb.shape[0] * 4 + 4096 * 2
+    res["rmsnorm_quant_int8_bf16_16384x4096"] = {"us": us, "GBps": nb / us / 1e3,
+                                                 "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    # prefill-size fused RoPE + paged append: 16384 new tokens into the decode cache layout
+    cache = WL.paged_cache(num_blocks=16384, block_size=BS, Hkv=HKV, D=D, device=dev, seed=9)
+    app = WL.decode_append_inputs(cache, n_tok=16384, Hq=HQ, device=dev, seed=9)
+    q_out = torch.empty_like(app["q"])
+    us = _median_us(lambda: K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"],
+                                                   app["sin"], app["slot_mapping"], cache.k_cache, cache.v_cache,
+                                                   q_out=q_out), flush_l2=True)
+    nb = WL.append_bytes(16384, HQ, HKV, D)
+    res["rope_kv_append_paged_prefill_16384tok"] = {"us": us, "GBps": nb / us / 1e3,
+                                                    "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
     return res
 
 

@@ -88,6 +88,23 @@ int b200_rmsnorm(const void* x, const void* weight, void* y, int64_t rows,
                  int64_t D, float eps, int32_t dtype, int32_t weight_dtype,
                  const b200_launch_cfg* cfg, void* stream);
 
+/* ---- rmsnorm fused with the INT8 activation quantiser ----------------------
+ * Composition of triton_agent/ops/rmsnorm/reference.py:17-18 and the row
+ * quantiser of triton_agent/ops/quant_matmul/reference.py:16-19 (the step
+ * before the INT8 GEMM in a decode layer): y = rmsnorm(x, weight) rounded to
+ * `dtype` (as b200_rmsnorm writes it), scale[r] = max|y[r,:]| / 127 rounded
+ * to `dtype` (0 -> 1e-6), q = clamp(round_half_even(y / scale), -127, 127).
+ * The codes and scales are bit-identical to b200_quantize_int8 (row mode)
+ * of the normalised rows computed here (returned in y when non-null); those
+ * equal b200_rmsnorm's output up to the order of the fp32 sum of squares.
+ * One pass over x.  q: [rows, D] int8 (8-byte aligned); scale: [rows]
+ * f32; y (nullable): [rows, D] of `dtype`.  Needs D % (16 / sizeof(dtype))
+ * == 0 and 16-byte aligned x/weight/y (B200_ERR_ALIGNMENT otherwise). */
+int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t* q, float* scale,
+                            void* y, int64_t rows, int64_t D, float eps, int32_t dtype,
+                            int32_t weight_dtype, const b200_launch_cfg* cfg, void* stream);
+
+
 /* ---- RoPE (NeoX rotate-half) ---------------------------------------------
  * Replaces triton_agent/ops/rope/reference.py:6-25
  * x, y: [B, H, T, D]; cos, sin: [T, D] of `cs_dtype` (first D/2 columns used).

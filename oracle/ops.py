@@ -339,3 +339,13 @@ def flash_attn(q, k, v, causal: bool = False, rows: slice | None = None, chunk: 
     if rows is None:
         return out.reshape(B, H, T, D)
     return out
+
+
+# ---------------------------------------------------------- rmsnorm + quant
+def rmsnorm_quant_int8(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6):
+    """rmsnorm (triton_agent/ops/rmsnorm/reference.py:17-18, fp32, cast to
+    x's dtype) followed by the row quantiser of
+    triton_agent/ops/quant_matmul/reference.py:16-19.  Returns (q int8,
+    scale in x's dtype [rows, 1])."""
+    y = rmsnorm(x, weight, eps)
+    return quantize_int8(y.reshape(-1, y.shape[-1]))

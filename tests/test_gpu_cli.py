@@ -27,6 +27,8 @@ CASES = [
     ("quant_matmul", "B=1,M=300,K=1024,N=512", "fp32"),
     ("flash_attn_like", "B=1,H=4,T=256,S=256,D=64", "bf16"),
     ("flash_attn_like", "B=1,H=2,T=384,S=384,D=128", "fp16"),
+    ("rmsnorm_quant", "B=2,T=64,D=4096", "bf16"),
+    ("rmsnorm_quant", "B=3,T=5,D=1024", "fp32"),
 ]
 
 

@@ -1,0 +1,73 @@
+"""GPU parity: rmsnorm fused with the row INT8 quantiser.  Codes and scales
+are bit-identical to b200_quantize_int8 of the normalised rows the kernel
+produces (the warp-per-row kernel divides by Markstein's correction step
+instead of an IEEE division; the 8x2048x4096 case checks it against the
+division on 2^26 values), the rows equal b200_rmsnorm's up to the order of
+the fp32 sum of squares, and against the oracle composition
+(rmsnorm in fp32 cast to the dtype, then the reference quantiser) the codes
+move by at most one step where a half-precision rounding of y differs."""
+
+import pytest
+import torch
+
+import oracle.ops as O
+from b200ops.runtime import lib as L
+from b200ops.runtime import ops as K
+
+pytestmark = pytest.mark.gpu
+
+
+def inputs(rows, D, dtype, wdtype, dev, seed=0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(rows, D, generator=g, device=dev).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(D, generator=g, device=dev)).to(wdtype)
+    return x, w
+
+
+@pytest.mark.parametrize("rows,D,dtype,wdtype", [
+    (16, 4096, torch.bfloat16, torch.bfloat16), (37, 4104, torch.bfloat16, torch.float32),
+    (64, 4096, torch.float16, torch.float16), (9, 1000, torch.float32, torch.float32),
+    (8 * 2048, 4096, torch.bfloat16, torch.bfloat16), (5, 64, torch.float16, torch.float32),
+])
+@pytest.mark.parametrize("cfg", [None, {"threads": 256}])  # warp-per-row kernel / CTA-per-row kernel
+def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
+    x, w = inputs(rows, D, dtype, wdtype, cuda_device)
+    q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg=cfg)
+    # the codes and scales are exactly the quantiser's on the y this kernel produced
+    q_ref, s_ref = K.quantize_int8(y)
+    torch.cuda.synchronize()
+    assert torch.equal(q, q_ref)
+    assert torch.equal(s, s_ref.reshape(-1).float())
+    # y is b200_rmsnorm's output up to the order of the fp32 sum of squares
+    # (identical when both reduce in the same order: the CTA-per-row kernel)
+    y_ref = K.rmsnorm(x, w, 1e-6)
+    if cfg is not None:
+        assert torch.equal(y, y_ref)
+    else:
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        torch.testing.assert_close(y.float(), y_ref.float(), rtol=tol, atol=tol)
+    q2, s2 = K.rmsnorm_quant_int8(x, w, 1e-6, cfg=cfg)  # without y
+    assert torch.equal(q2, q) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_against_oracle_composition(dtype, cuda_device):
+    x, w = inputs(24, 4096, dtype, dtype, cuda_device, seed=3)
+    q, s = K.rmsnorm_quant_int8(x, w, 1e-6)
+    qo, so = O.rmsnorm_quant_int8(x.cpu(), w.cpu(), 1e-6)
+    d = (q.cpu().int() - qo.int()).abs()
+    assert int(d.max()) <= 1
+    assert float((d == 0).float().mean()) > 0.99
+    torch.testing.assert_close(s.cpu(), so.reshape(-1).float(), rtol=1e-2, atol=0)
+
+
+def test_zero_rows_and_misaligned_width(cuda_device):
+    x = torch.zeros(4, 256, dtype=torch.bfloat16, device=cuda_device)
+    w = torch.ones(256, dtype=torch.bfloat16, device=cuda_device)
+    q, s = K.rmsnorm_quant_int8(x, w)
+    torch.cuda.synchronize()
+    assert int(q.abs().max()) == 0
+    assert torch.equal(s.cpu(), torch.full((4,), O.quantize_int8(torch.zeros(1, 8, dtype=torch.bfloat16))[1].float().item()))
+    xb, wb = inputs(4, 4100, torch.bfloat16, torch.bfloat16, cuda_device)
+    with pytest.raises(L.B200OpsError):
+        K.rmsnorm_quant_int8(xb, wb)

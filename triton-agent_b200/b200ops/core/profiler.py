@@ -4,7 +4,9 @@ The reference times each call with host perf_counter around a device
 synchronize, which folds launch overhead and host jitter into every sample.
 Here each iteration is timed on the device with CUDA events recorded on the
 launching stream; with `flush_l2` a buffer larger than L2 is overwritten
-between iterations so memory-bound kernels are not served from cache.
+and then read back between iterations, so memory-bound kernels are not served
+from cache and the timed call does not pay for writing back the flush's
+dirty lines (the read evicts them before the start event).
 Reported fields are unchanged: p50/p90/p99 in microseconds, variance as the
 coefficient of variation, speedup against baseline_latency_us, and the peak
 allocated memory.
@@ -44,6 +46,7 @@ def time_device(fn: Callable[[], Any], warmup: int = 20, repeat: int = 100, flus
     for i in range(repeat):
         if flush is not None:
             flush.fill_(float(i))
+            flush.sum()  # leaves L2 holding clean lines of the flush buffer
         starts[i].record(stream)
         fn()
         ends[i].record(stream)

@@ -84,6 +84,26 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch
     return y
 
 
+def rmsnorm_quant_int8(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, want_y: bool = False, cfg=None):
+    """rmsnorm fused with the per-row INT8 quantiser of the next GEMM's
+    activations (rmsnorm/reference.py:17-18 then quant_matmul/reference.py:16-19).
+    Returns (q int8 [..., D], scale f32 [rows]) or (q, scale, y) with want_y."""
+    dev = _need_cuda("rmsnorm_quant_int8", x, weight)
+    _contig("rmsnorm_quant_int8", x=x, weight=weight)
+    D = x.shape[-1]
+    if weight.numel() != D:
+        raise L.B200OpsError(L.ERR_BAD_ARG, "rmsnorm_quant_int8", "weight must have D elements")
+    rows = x.numel() // D if D else 0
+    q = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    scale = torch.empty(rows, dtype=torch.float32, device=dev)
+    y = torch.empty_like(x) if want_y else None
+    st = L.load().b200_rmsnorm_quant_int8(_ptr(x), _ptr(weight), _ptr(q), _ptr(scale), _ptr(y), rows, D,
+                                          float(eps), dtype_code(x.dtype), dtype_code(weight.dtype), _cfg(cfg),
+                                          _stream(dev))
+    L.check(st, "rmsnorm_quant_int8")
+    return (q, scale, y) if want_y else (q, scale)
+
+
 # ------------------------------------------------------------------------ RoPE
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor | None = None,
          cfg=None) -> torch.Tensor:

@@ -165,6 +165,29 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---- symmetric INT8 quantisation of one value (quant_matmul/reference.py:16-24)
+// Eager PyTorch divides in fp32 and rounds the quotient to x's dtype before
+// round() (half to even); the scale max|x|/127 is rounded to that dtype too.
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return to_f32(from_f32<T>(v));
+}
+
+template <typename T>
+__device__ __forceinline__ int8_t quant_one(float x, float s) {
+  float qv = round_to<T>(__fdiv_rn(x, s));
+  qv = rintf(qv);
+  qv = fminf(fmaxf(qv, -127.f), 127.f);
+  return (int8_t)(int)qv;
+}
+
+template <typename T>
+__device__ __forceinline__ float finish_scale(float amax) {
+  float s = round_to<T>(__fdiv_rn(amax, 127.0f));
+  if (s == 0.f) s = round_to<T>(1e-6f);
+  return s;
+}
+
 }  // namespace b200
 
 // Dispatches a float dtype code to a C++ type alias `scalar_t`.

@@ -13,26 +13,6 @@
 namespace b200 {
 namespace {
 
-template <typename T>
-__device__ __forceinline__ float round_to(float v) {
-  return to_f32(from_f32<T>(v));
-}
-
-template <typename T>
-__device__ __forceinline__ int8_t quant_one(float x, float s) {
-  float qv = round_to<T>(__fdiv_rn(x, s));
-  qv = rintf(qv);
-  qv = fminf(fmaxf(qv, -127.f), 127.f);
-  return (int8_t)(int)qv;
-}
-
-template <typename T>
-__device__ __forceinline__ float finish_scale(float amax) {
-  float s = round_to<T>(__fdiv_rn(amax, 127.0f));
-  if (s == 0.f) s = round_to<T>(1e-6f);
-  return s;
-}
-
 // One CTA per row.
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x,
