@@ -198,6 +198,21 @@ def secondary_ops(dev) -> dict:
     us = _median_us(lambda: K.rmsnorm(x, w, out=y), flush_l2=True)
     nb = 2 * x.numel() * 4 + 4096 * 4
     res["rmsnorm_fp32_8x2048x4096"] = {"us": us, "GBps": nb / us / 1e3, "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    # matmul_epilogue: fp16 [8*256, 4096] x [4096, 4096] + bias, GELU
+    g = torch.Generator(device=dev).manual_seed(11)
+    a_e = (torch.randn(8 * 256, 4096, generator=g, device=dev) / 8).half()
+    b_e = torch.randn(4096, 4096, generator=g, device=dev).half()
+    bias_e = torch.randn(4096, generator=g, device=dev).half()
+    us = _median_us(lambda: K.gemm_bias_gelu(a_e, b_e, bias_e), flush_l2=True)
+    fl = 2 * 2048 * 4096 * 4096
+    res["matmul_epilogue_fp16_2048x4096x4096"] = {"us": us, "TFLOPs": fl / us / 1e6,
+                                                  "frac": fl / us / 1e6 / peaks["bf16_tflops"]}
+    try:
+        us_cb = _median_us(lambda: torch.nn.functional.gelu(torch.addmm(bias_e, a_e, b_e), approximate="tanh"),
+                           flush_l2=True)
+        res["matmul_epilogue_fp16_2048x4096x4096"]["torch_cublas_addmm_gelu_TFLOPs"] = fl / us_cb / 1e6
+    except Exception:
+        pass
     # rmsnorm fused with the INT8 activation quantiser (bf16 in, int8 codes + f32 row scales out)
     xb, wb = x.bfloat16().reshape(-1, 4096), w.bfloat16()
     us = _median_us(lambda: K.rmsnorm_quant_int8(xb, wb), flush_l2=True)

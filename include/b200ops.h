@@ -231,6 +231,18 @@ int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,
                    void* workspace, size_t workspace_bytes,
                    const b200_launch_cfg* cfg, void* stream);
 
+/* ---- bf16/fp16 GEMM + bias + GELU ------------------------------------------
+ * Replaces triton_agent/ops/matmul_epilogue/reference.py:6-18
+ *   c = gelu_tanh(a @ b + bias)
+ * a: [M, K] (the reference's [B, M, K] flattened), b: [K, N] row-major (as
+ * the reference passes it), bias: [N], c: [M, N], all of `dtype` (F16 or
+ * BF16).  fp32 accumulation in tensor memory (tcgen05 kind::f16, CTA pairs),
+ * bias and GELU (tanh form) in fp32, one rounding to `dtype`.  Needs
+ * K % 8 == 0, N % 8 == 0 and 16-byte aligned a, b, c. */
+int b200_gemm_bias_gelu(const void* a, const void* b, const void* bias, void* c, int64_t M,
+                        int64_t N, int64_t K, int32_t dtype, const b200_launch_cfg* cfg,
+                        void* stream);
+
 /* ---- column-sharded INT8 GEMM with the all-gather fused (multi-GPU) --------
  * No counterpart in the reference (which runs on one device): the
  * multi-GPU layout of quant_matmul partitions W by output columns, and

@@ -349,3 +349,11 @@ def rmsnorm_quant_int8(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6)
     scale in x's dtype [rows, 1])."""
     y = rmsnorm(x, weight, eps)
     return quantize_int8(y.reshape(-1, y.shape[-1]))
+
+
+# --------------------------------------------------------- matmul epilogue
+def matmul_epilogue(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """triton_agent/ops/matmul_epilogue/reference.py:6-18 in fp32:
+    c = a @ b + bias; 0.5 c (1 + tanh(0.7978845608028654 (c + 0.044715 c^3)))."""
+    c = a.detach().cpu().float() @ b.detach().cpu().float() + bias.detach().cpu().float()
+    return 0.5 * c * (1.0 + torch.tanh(0.7978845608028654 * (c + 0.044715 * c.pow(3))))

@@ -16,7 +16,7 @@ from b200ops.core.verifier import check_numerical
 from b200ops.ops import OPS_DIR
 
 HOT_OPS = ["rmsnorm", "rope", "kv_append", "paged_kv", "rope_kv_append", "rope_kv_append_paged", "paged_attention",
-           "quant_matmul", "flash_attn_like", "rmsnorm_quant"]
+           "quant_matmul", "flash_attn_like", "rmsnorm_quant", "matmul_epilogue"]
 
 
 def minimal(**over):

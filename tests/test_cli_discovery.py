@@ -9,7 +9,7 @@ from b200ops.core.spec import OpAction, OpState
 from b200ops.ops._variant import launch_cfg_from_args
 
 HOT_OPS = ["rmsnorm", "rope", "kv_append", "paged_kv", "rope_kv_append", "rope_kv_append_paged", "paged_attention",
-           "quant_matmul", "flash_attn_like", "rmsnorm_quant"]
+           "quant_matmul", "flash_attn_like", "rmsnorm_quant", "matmul_epilogue"]
 
 
 def test_discovery_per_op():

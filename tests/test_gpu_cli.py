@@ -29,6 +29,8 @@ CASES = [
     ("flash_attn_like", "B=1,H=2,T=384,S=384,D=128", "fp16"),
     ("rmsnorm_quant", "B=2,T=64,D=4096", "bf16"),
     ("rmsnorm_quant", "B=3,T=5,D=1024", "fp32"),
+    ("matmul_epilogue", "B=2,M=256,K=1024,N=768", "fp16"),
+    ("matmul_epilogue", "B=1,M=300,K=512,N=264", "bf16"),
 ]
 
 

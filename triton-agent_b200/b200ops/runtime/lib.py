@@ -101,6 +101,7 @@ SIGNATURES = {
     ),
     "b200_int8_gemm_workspace_size": (c_size_t, [I64_, I64_, I64_, PCFG]),
     "b200_int8_gemm": (c_int, [P, P, P, P, P, I64_, I64_, I64_, I64_, c_int32, P, P, c_size_t, PCFG, P]),
+    "b200_gemm_bias_gelu": (c_int, [P, P, P, P, I64_, I64_, I64_, c_int32, PCFG, P]),
     "b200_int8_gemm_allgather": (
         c_int,
         [P, P, P, P, POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int32, I64_, I64_, I64_, I64_, I64_, c_int32,

@@ -282,6 +282,24 @@ def int8_gemm(A: torch.Tensor, W: torch.Tensor, sA: torch.Tensor, sW: torch.Tens
     return C
 
 
+def gemm_bias_gelu(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor, out: torch.Tensor | None = None,
+                   cfg=None) -> torch.Tensor:
+    """gelu_tanh(a @ b + bias) (matmul_epilogue/reference.py:6-18): a [..., M, K],
+    b [K, N], bias [N], fp16 or bf16; fp32 accumulation and epilogue."""
+    dev = _need_cuda("gemm_bias_gelu", a, b, bias, out)
+    _contig("gemm_bias_gelu", a=a, b=b, bias=bias, out=out)
+    K = a.shape[-1]
+    if b.dim() != 2 or b.shape[0] != K or bias.numel() != b.shape[1] or not (a.dtype == b.dtype == bias.dtype):
+        raise L.B200OpsError(L.ERR_BAD_ARG, "gemm_bias_gelu", "a [..., M, K], b [K, N], bias [N] of one dtype")
+    N = b.shape[1]
+    M = a.numel() // K if K else 0
+    c = torch.empty(*a.shape[:-1], N, dtype=a.dtype, device=dev) if out is None else out
+    st = L.load().b200_gemm_bias_gelu(_ptr(a), _ptr(b), _ptr(bias), _ptr(c), M, N, K, dtype_code(a.dtype),
+                                      _cfg(cfg), _stream(dev))
+    L.check(st, "gemm_bias_gelu")
+    return c
+
+
 def quantize_int8(x: torch.Tensor, by_column: bool = False, cfg=None):
     """Per-row (or per-column, transposed) symmetric int8 quantisation
     (quant_matmul/reference.py:16-24).  Returns (q int8, scale f32)."""

@@ -61,6 +61,7 @@ struct GemmParams {
   int world, self;
   int64_t col_off;
   void* dst[kMaxRanks];
+  const void* bias;     // bias + GELU flavour: [N] of the output type
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -177,6 +178,35 @@ __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int l
     }
   }
   __syncwarp();
+}
+
+// GELU with the tanh approximation of matmul_epilogue/reference.py:17,
+// 0.5 c (1 + tanh(sqrt(2/pi) (c + 0.044715 c^3))), in fp32 with the
+// hardware tanh (tanh.approx.f32, relative error ~2^-11, below the bf16/fp16
+// rounding of the output).
+__device__ __forceinline__ float gelu_tanh(float c) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * c, c * c, c);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * c * (1.0f + t);
+}
+
+// fp32 accumulators of one row + bias, GELU, one rounding to OutT.
+template <typename OutT>
+__device__ __forceinline__ void bias_gelu_chunk(const uint32_t* acc, int64_t row, int64_t col0,
+                                                OutT* __restrict__ C, const GemmParams& p) {
+  const int64_t rem = p.N - col0;
+  const int n_valid = rem < 32 ? (int)rem : 32;
+  if (n_valid <= 0) return;
+  const OutT* bias = static_cast<const OutT*>(p.bias);
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float b = (j < n_valid) ? to_f32(bias[col0 + j]) : 0.f;
+    v[j] = gelu_tanh(__uint_as_float(acc[j]) + b);
+  }
+  OutT* dst = C + row * p.ldc + col0;
+  store_out_row<OutT>(dst, v, n_valid, (reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
 }
 
 // Shared-memory carve-up of both kernels: [ring of stages][barriers...]
@@ -413,7 +443,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ----------------------------------------------------------------------------
 constexpr int kPairN = 256;
 
-template <typename OutT>
+// kF16: the bf16/fp16 flavour (kind::f16, fp32 accumulators, B = b [K, N]
+// N-contiguous, i.e. MN-major: per CTA two TMA boxes of 64 N x 64 K, 8 KB
+// apart; epilogue bias + GELU) -- same pipeline, same 32 KB stages, same
+// 32-byte K step per MMA.
+template <typename OutT, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                           const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
@@ -471,8 +505,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (rank == 0) sm100::mbar_arrive_expect_tx(fb, 2 * p.stage_bytes);  // both CTAs' fills
           const uint32_t fb0 = sm100::mapa_shared(fb, 0);
           const uint32_t dst = base + s * p.stage_bytes;
-          sm100::tma_load_2d_pair(dst, &tm_a, fb0, kt * BK, a_row);
-          sm100::tma_load_2d_pair(dst + p.a_bytes, &tm_b, fb0, kt * BK, b_row);
+          if constexpr (kF16) {
+            // 64 elements of K per stage; b [K, N]: boxes {64 N, 64 K} at N offsets 0 and 64
+            sm100::tma_load_2d_pair(dst, &tm_a, fb0, kt * 64, a_row);
+            sm100::tma_load_2d_pair(dst + p.a_bytes, &tm_b, fb0, b_row, kt * 64);
+            sm100::tma_load_2d_pair(dst + p.a_bytes + 8192, &tm_b, fb0, b_row + 64, kt * 64);
+          } else {
+            sm100::tma_load_2d_pair(dst, &tm_a, fb0, kt * BK, a_row);
+            sm100::tma_load_2d_pair(dst + p.a_bytes, &tm_b, fb0, kt * BK, b_row);
+          }
         }
       }
       if (!ok) set_abort(bars, kDevErrTimeoutEmpty);
@@ -482,10 +523,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (rank == 0) {
       // MMA issue for the pair: the whole warp runs the loop, one elected lane issues
-      constexpr uint32_t idesc = sm100::make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, 0, 0, 2 * BM, kPairN);
+      // D s32 from s8 x s8, or D f32 from bf16 (1) / fp16 (0) with B MN-major
+      constexpr uint32_t ab_fmt = kF16 ? (std::is_same<OutT, __nv_bfloat16>::value ? 1u : 0u) : 1u;
+      constexpr uint32_t idesc =
+          sm100::make_idesc(kF16 ? 1u : 2u, ab_fmt, ab_fmt, 0, kF16 ? 1u : 0u, 2 * BM, kPairN);
       const uint32_t leader = sm100::elect_one();
       const uint64_t ad0 = sm100::make_smem_desc(base, 16, 1024, sm100::kSwizzle128B);
-      const uint64_t bd0 = sm100::make_smem_desc(base + p.a_bytes, 16, 1024, sm100::kSwizzle128B);
+      // B: K-major (K steps of 32 B inside the atom) or MN-major (the two
+      // 64-wide N halves 8 KB apart = LBO; K steps of 16 rows x 128 B)
+      const uint64_t bd0 = kF16 ? sm100::make_smem_desc(base + p.a_bytes, 8192, 1024, sm100::kSwizzle128B)
+                                : sm100::make_smem_desc(base + p.a_bytes, 16, 1024, sm100::kSwizzle128B);
+      constexpr uint32_t b_step = kF16 ? 2048 >> 4 : 2;
       const uint32_t empty0 = sm100::smem_u32(&bars.empty[0]);
       const uint32_t empty_r0 = sm100::mapa_shared(empty0, 0), empty_r1 = sm100::mapa_shared(empty0, 1);
       const uint32_t accf0 = sm100::smem_u32(&bars.acc_full[0]);
@@ -510,9 +558,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm100::tc_fence_after();
           const uint64_t so = (uint64_t)((r.s * p.stage_bytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / 32; ++kk)
-            sm100::mma_i8_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u,
-                                  leader);
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            if constexpr (kF16)
+              sm100::mma_f16_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + b_step * kk, idesc,
+                                     (kt > 0 || kk > 0) ? 1u : 0u, leader);
+            else
+              sm100::mma_i8_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + b_step * kk, idesc,
+                                    (kt > 0 || kk > 0) ? 1u : 0u, leader);
+          }
           sm100::tc_commit_pair(empty_r0 + 8 * r.s, leader);
           sm100::tc_commit_pair(empty_r1 + 8 * r.s, leader);
         }
@@ -542,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < kPairN;) {
         const int64_t col0 = (int64_t)n_tile * kPairN + c;
-        if constexpr (sizeof(OutT) == 2) {
+        if constexpr (sizeof(OutT) == 2 && !kF16) {
           if (p.world > 1 && col0 + kGatherCols <= p.N) {  // warp-uniform
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes);
@@ -553,7 +606,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc[32];
         sm100::tmem_ld_32x32b_x32(t_row + c, acc);
         sm100::tmem_wait_ld_regs(acc);
-        if (row < p.M && !aborted(bars)) epilogue_chunk<OutT>(acc, row, col0, sA, sW, C, acc_out, p);
+        if (row < p.M && !aborted(bars)) {
+          if constexpr (kF16)
+            bias_gelu_chunk<OutT>(acc, row, col0, C, p);
+          else
+            epilogue_chunk<OutT>(acc, row, col0, sA, sW, C, acc_out, p);
+        }
         c += 32;
       }
       sm100::tc_fence_before();
@@ -981,29 +1039,34 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
   return g;
 }
 
+// CTA-pair kernel launch: clusters of two CTAs (cudaLaunchKernelEx).
+template <typename OutT, bool kF16>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
+                int32_t* acc_out, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
+  auto kern = int8_gemm_pair_kernel<OutT, kF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+  if (e != cudaSuccess) return launch_status(e);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)g.grid);
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = g.smem;
+  lc.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  e = cudaLaunchKernelEx(&lc, kern, ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, p);
+  if (e != cudaSuccess) return launch_status(e);
+  return launch_status(cudaGetLastError());
+}
+
 template <typename OutT>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
            int32_t* acc_out, void* ws, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
-  if (g.pair) {
-    auto kern = int8_gemm_pair_kernel<OutT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
-    if (e != cudaSuccess) return launch_status(e);
-    cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3((unsigned)g.grid);
-    lc.blockDim = dim3(kThreads);
-    lc.dynamicSmemBytes = g.smem;
-    lc.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    lc.attrs = at;
-    lc.numAttrs = 1;
-    e = cudaLaunchKernelEx(&lc, kern, ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, p);
-    if (e != cudaSuccess) return launch_status(e);
-    return launch_status(cudaGetLastError());
-  }
+  if (g.pair) return launch_pair<OutT, false>(ta, tb, sA, sW, C, acc_out, g, p, s);
   if (!g.skinny) {
     auto kern = g.BN == 256 ? int8_gemm_tcgen05_kernel<256, OutT> : int8_gemm_tcgen05_kernel<128, OutT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
@@ -1191,3 +1254,72 @@ extern "C" int b200_int8_gemm_allgather(const int8_t* A, const int8_t* W_local, 
   return launch_status(cudaGetLastError());
 }
 
+
+// ---------------------------------------------------------------------------
+// bf16/fp16 GEMM + bias + GELU (matmul_epilogue): the CTA-pair kernel's
+// kind::f16 flavour.
+// ---------------------------------------------------------------------------
+extern "C" int b200_gemm_bias_gelu(const void* a, const void* b, const void* bias, void* c, int64_t M, int64_t N,
+                                   int64_t K, int32_t dtype, const b200_launch_cfg* cfg, void* stream) {
+  using namespace b200;
+  if (int e = injected_error("gemm_bias_gelu")) return e;
+  if (M < 0 || N < 0 || K < 0) return B200_ERR_BAD_ARG;
+  if (M == 0 || N == 0) return B200_OK;
+  if (!a || !b || !bias || !c || K == 0) return B200_ERR_BAD_ARG;
+  if (dtype != B200_BF16 && dtype != B200_F16) return B200_ERR_UNSUPPORTED;
+  if (K % 8 != 0 || N % 8 != 0) return B200_ERR_UNSUPPORTED;  // 16-byte TMA row pitches
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return B200_ERR_ALIGNMENT;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
+  const int sms = device_sm_count();
+  if (sms < 2) return B200_ERR_NO_DEVICE;
+  GemmPlan g{};
+  g.pair = true;
+  g.BN = kPairN;
+  g.k_tiles = (int)((K + 63) / 64);  // 64 elements (128 B) of K per stage
+  g.m_tiles = (int)((M + 2 * BM - 1) / (2 * BM));
+  g.n_tiles = (int)((N + kPairN - 1) / kPairN);
+  g.splits = 1;
+  g.k_tiles_split = g.k_tiles;
+  g.a_bytes = BM * 128;
+  g.stage_bytes = g.a_bytes + 2 * 8192;
+  const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
+  g.grid = 2 * (int)(tiles < sms / 2 ? tiles : sms / 2);
+  // shared memory as in plan_gemm: stages, carve()'s barrier block, 1 KB alignment slack
+  auto bar_bytes = [](int st) -> size_t { return (size_t)(2 * st + 5) * 8 + 16; };
+  int stages = (cfg && cfg->stages > 0) ? cfg->stages : 8;
+  while (stages > 2 && (size_t)stages * g.stage_bytes + bar_bytes(stages) > 227 * 1024 - 1024) --stages;
+  g.stages = stages;
+  g.smem = (size_t)stages * g.stage_bytes + bar_bytes(stages) + 1024;
+  const CUtensorMapDataType dt = dtype == B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, BM};
+    if (int st = encode_tensor_map(&ta, dt, 2, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)N * 2};
+    const uint32_t box[2] = {64, 64};
+    if (int st = encode_tensor_map(&tb, dt, 2, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = N;
+  p.k_tiles = g.k_tiles;
+  p.k_tiles_split = g.k_tiles;
+  p.splits = 1;
+  p.stages = g.stages;
+  p.m_tiles = g.m_tiles;
+  p.n_tiles = g.n_tiles;
+  p.num_tiles = g.m_tiles * g.n_tiles;
+  p.stage_bytes = g.stage_bytes;
+  p.a_bytes = g.a_bytes;
+  p.bias = bias;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_BF16) return launch_pair<__nv_bfloat16, true>(ta, tb, nullptr, nullptr, c, nullptr, g, p, s);
+  return launch_pair<__half, true>(ta, tb, nullptr, nullptr, c, nullptr, g, p, s);
+}
