@@ -22,3 +22,25 @@ def test_quantize_codes_exact(dtype, shape, by_column, cuda_device):
     eq, es = O.quantize_int8(x, by_column=by_column)
     assert torch.equal(q.cpu(), eq)
     assert torch.equal(s.cpu(), es.float())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_quantize_codes_exact_at_scale_and_ties(dtype, cuda_device):
+    """2048 rows x 4096: random rows of many magnitudes, and rows whose scale
+    is a power of two with entries on the half-integer ties of x / scale
+    (round half to even) and just beside them -- the codes must match the
+    reference rounding everywhere."""
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(2048, 4096, generator=g) * torch.exp2(torch.randint(-12, 8, (2048, 1), generator=g).float())
+    k = torch.randint(-127, 127, (512, 4096), generator=g).float() + 0.5
+    e = torch.exp2(torch.randint(-10, 4, (512, 1), generator=g).float())
+    ties = k * e
+    ties[:, 0] = 127 * e[:, 0]  # row max: scale = e exactly
+    nudge = torch.where(torch.rand(512, 4096, generator=g) < 0.5, 1 - 2.0 ** -7, 1 + 2.0 ** -7)
+    x[:512] = ties
+    x[512:1024] = ties * nudge
+    x = x.to(dtype)
+    q, s = K.quantize_int8(x.to(cuda_device))
+    eq, es = O.quantize_int8(x)
+    assert torch.equal(s.cpu(), es.float().reshape(-1))
+    assert torch.equal(q.cpu(), eq)

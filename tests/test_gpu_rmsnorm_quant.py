@@ -1,8 +1,6 @@
 """GPU parity: rmsnorm fused with the row INT8 quantiser.  Codes and scales
 are bit-identical to b200_quantize_int8 of the normalised rows the kernel
-produces (the warp-per-row kernel divides by Markstein's correction step
-instead of an IEEE division; the 8x2048x4096 case checks it against the
-division on 2^26 values), the rows equal b200_rmsnorm's up to the order of
+produces, the rows equal b200_rmsnorm's up to the order of
 the fp32 sum of squares, and against the oracle composition
 (rmsnorm in fp32 cast to the dtype, then the reference quantiser) the codes
 move by at most one step where a half-precision rounding of y differs."""
@@ -29,7 +27,7 @@ def inputs(rows, D, dtype, wdtype, dev, seed=0):
     (64, 4096, torch.float16, torch.float16), (9, 1000, torch.float32, torch.float32),
     (8 * 2048, 4096, torch.bfloat16, torch.bfloat16), (5, 64, torch.float16, torch.float32),
 ])
-@pytest.mark.parametrize("cfg", [None, {"threads": 256}])  # warp-per-row kernel / CTA-per-row kernel
+@pytest.mark.parametrize("cfg", [None, {"threads": 256}])  # default CTA size / b200_rmsnorm's for D=4096
 def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
     x, w = inputs(rows, D, dtype, wdtype, cuda_device)
     q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg=cfg)
@@ -39,7 +37,7 @@ def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
     assert torch.equal(q, q_ref)
     assert torch.equal(s, s_ref.reshape(-1).float())
     # y is b200_rmsnorm's output up to the order of the fp32 sum of squares
-    # (identical when both reduce in the same order: the CTA-per-row kernel)
+    # (identical when both reduce in the same order: the same CTA size)
     y_ref = K.rmsnorm(x, w, 1e-6)
     if cfg is not None:
         assert torch.equal(y, y_ref)

@@ -5,6 +5,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <type_traits>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -179,6 +180,40 @@ __device__ __forceinline__ int8_t quant_one(float x, float s) {
   qv = rintf(qv);
   qv = fminf(fmaxf(qv, -127.f), 127.f);
   return (int8_t)(int)qv;
+}
+
+// The same code without the conversion pipe (which runs at a fraction of the
+// ALU rate and bounds a quantiser otherwise): x / s by Markstein's correction
+// step (P. Markstein, IBM J. Res. Dev. 1990) from r = 1/s correctly rounded,
+// q0 = RN(x r), e = x - q0 s exactly, RN(q0 + e r) = RN(x / s); rounding to
+// T's precision on the bits (round half to even; for fp16 values below its
+// normal range the result only feeds the integer rounding, which gives 0
+// either way); round half to even to an integer by adding 1.5 * 2^23 (exact
+// for |v| < 2^22); clamp in integers.  Bit-identical to quant_one.
+template <typename T>
+__device__ __forceinline__ float round_bits_to(float v) {
+  if constexpr (std::is_same<T, float>::value) {
+    return v;
+  } else {
+    uint32_t u = __float_as_uint(v);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      u += 0x7FFFu + ((u >> 16) & 1u);
+      u &= 0xFFFF0000u;
+    } else {
+      u += 0xFFFu + ((u >> 13) & 1u);
+      u &= 0xFFFFE000u;
+    }
+    return __uint_as_float(u);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ int quant_code_fast(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q0, s, x);
+  const float qt = round_bits_to<T>(__fmaf_rn(e, r, q0));
+  const int i = __float_as_int(__fadd_rn(qt, 12582912.0f)) - 0x4B400000;
+  return max(-127, min(127, i));
 }
 
 template <typename T>

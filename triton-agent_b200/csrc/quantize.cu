@@ -5,8 +5,8 @@
 //   scale[scale == 0] = 1e-6
 //   q = clamp(round(x / scale), -127, 127).to(int8)
 // Eager PyTorch evaluates x / scale in fp32 and rounds the quotient to x's
-// dtype before round() (half-to-even); the kernels do the same, so the int8
-// codes are bit-identical.  The scale is returned as fp32 (exact widening of
+// dtype before round() (half-to-even); the kernels do the same (quant_code_fast,
+// common.cuh), so the int8 codes are bit-identical.  The scale is returned as fp32 (exact widening of
 // the dtype-rounded value).
 #include "common.cuh"
 
@@ -35,9 +35,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   }
   __syncthreads();
   const float s = finish_scale<T>(red[0]);
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[blockIdx.x] = s;
   int8_t* qr = q + (int64_t)blockIdx.x * cols;
-  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) qr[i] = quant_one<T>(to_f32(xr[i]), s);
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) qr[i] = (int8_t)quant_code_fast<T>(to_f32(xr[i]), s, rs);
 }
 
 // One CTA per 32 columns of x [rows, cols]; writes q transposed [cols, rows].
@@ -48,6 +49,7 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(const T* __restrict_
                                                             int64_t rows, int64_t cols) {
   __shared__ float red[8][33];
   __shared__ float s_scale[32];
+  __shared__ float s_rcp[32];
   __shared__ int8_t tile[32][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + lane;
@@ -61,6 +63,7 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(const T* __restrict_
     for (int w = 0; w < 8; ++w) v = fmaxf(v, red[w][lane]);
     const float s = finish_scale<T>(v);
     s_scale[lane] = s;
+    s_rcp[lane] = __frcp_rn(s);
     if (c < cols) scale[c] = s;
   }
   __syncthreads();
@@ -68,7 +71,8 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(const T* __restrict_
     // load a 32x32 tile (rows r0.., columns of this CTA), quantise
     for (int rr = warp; rr < 32; rr += 8) {
       const int64_t r = r0 + rr;
-      tile[rr][lane] = (r < rows && c < cols) ? quant_one<T>(to_f32(x[r * cols + c]), s_scale[lane]) : 0;
+      tile[rr][lane] =
+          (r < rows && c < cols) ? (int8_t)quant_code_fast<T>(to_f32(x[r * cols + c]), s_scale[lane], s_rcp[lane]) : 0;
     }
     __syncthreads();
     // write transposed: q[col][r0 + lane]

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_row_kernel(const T* __rest
     }
   }
   const float s = finish_scale<T>(block_max(amax, red2));
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[row] = s;
   int8_t* qr = q + row * D;
 #pragma unroll
@@ -153,96 +154,8 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_row_kernel(const T* __rest
       unpack16<T>(raw[i], f);
       int8_t c[VN];
 #pragma unroll
-      for (int j = 0; j < VN; ++j) c[j] = quant_one<T>(f[j], s);
+      for (int j = 0; j < VN; ++j) c[j] = (int8_t)quant_code_fast<T>(f[j], s, rs);
       // VN codes: 8 bytes for 16-bit T, 4 for fp32
-      if constexpr (VN == 8) {
-        uint2 pk;
-        memcpy(&pk, c, 8);
-        *reinterpret_cast<uint2*>(qr + (int64_t)v * VN) = pk;
-      } else {
-        uint32_t pk;
-        memcpy(&pk, c, 4);
-        *reinterpret_cast<uint32_t*>(qr + (int64_t)v * VN) = pk;
-      }
-    }
-  }
-}
-
-// Warp-per-row variant for rows of at most 32 * 32 vectors (D <= 8192 at 16
-// bits): no block barriers, eight rows per CTA.  The per-element division
-// y / scale uses Markstein's correction step (P. Markstein, "Computation of
-// elementary functions on the IBM RISC System/6000 processor", 1990): with
-// r = 1/scale correctly rounded (__frcp_rn, once per row), q0 = RN(y * r),
-// e = y - q0 * scale exactly (one FMA), RN(q0 + e * r) is the correctly
-// rounded quotient -- the value the unfused quantiser's IEEE division gives.
-template <typename T>
-__device__ __forceinline__ int8_t quant_one_recip(float x, float s, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float e = __fmaf_rn(-q0, s, x);
-  float qv = round_to<T>(__fmaf_rn(e, r, q0));
-  qv = rintf(qv);
-  qv = fminf(fmaxf(qv, -127.f), 127.f);
-  return (int8_t)(int)qv;
-}
-
-template <typename T, typename W, int NV>
-__global__ void __launch_bounds__(256) rmsnorm_quant_warp_kernel(const T* __restrict__ x, const W* __restrict__ w,
-                                                                 int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                 T* __restrict__ y, int64_t rows, int D,
-                                                                 float eps) {
-  constexpr int VN = Vec<T>::N;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;  // whole warp
-  const T* xr = x + row * D;
-  const int nvec = D / VN;
-  uint4 raw[NV];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = lane + 32 * i;
-    if (v < nvec) {
-      raw[i] = ldg_stream16(xr + (int64_t)v * VN);
-      float f[VN];
-      unpack16<T>(raw[i], f);
-#pragma unroll
-      for (int j = 0; j < VN; ++j) ss = fmaf(f[j], f[j], ss);
-    }
-  }
-  ss = warp_sum(ss);
-  const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = lane + 32 * i;
-    if (v < nvec) {
-      float f[VN], wf[VN];
-      unpack16<T>(raw[i], f);
-      load_weights<W, VN>(w + (int64_t)v * VN, wf);
-#pragma unroll
-      for (int j = 0; j < VN; ++j) f[j] = __fmul_rn(__fmul_rn(f[j], rstd), wf[j]);
-      raw[i] = pack16<T>(f);  // y rounded to T
-      unpack16<T>(raw[i], f);
-#pragma unroll
-      for (int j = 0; j < VN; ++j) amax = fmaxf(amax, fabsf(f[j]));
-      if (y != nullptr) stg_stream16(y + row * D + (int64_t)v * VN, raw[i]);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float sc = finish_scale<T>(amax);
-  const float rc = __frcp_rn(sc);
-  if (lane == 0) scale[row] = sc;
-  int8_t* qr = q + row * D;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = lane + 32 * i;
-    if (v < nvec) {
-      float f[VN];
-      unpack16<T>(raw[i], f);
-      int8_t c[VN];
-#pragma unroll
-      for (int j = 0; j < VN; ++j) c[j] = quant_one_recip<T>(f[j], sc, rc);
       if constexpr (VN == 8) {
         uint2 pk;
         memcpy(&pk, c, 8);
@@ -365,24 +278,10 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     const int64_t nvec = D / VN;
     int threads = (cfg && cfg->threads > 0) ? cfg->threads : 0;
     if (threads != 0 && (threads < 32 || threads > 1024 || threads % 32 != 0)) return B200_ERR_BAD_ARG;
-    const T* xp0 = static_cast<const T*>(x);
-    const W* wp0 = static_cast<const W*>(weight);
-    T* yp0 = static_cast<T*>(y);
-    // a warp per row while the row fits 16 vectors per lane (cfg threads forces the CTA-per-row kernel)
-    if (threads == 0 && nvec <= 32 * 16) {
-      const int64_t nv = (nvec + 31) / 32;
-      const unsigned grid = (unsigned)((rows + 7) / 8);
-      if (nv <= 4)
-        rmsnorm_quant_warp_kernel<T, W, 4><<<grid, 256, 0, s>>>(xp0, wp0, q, scale, yp0, rows, (int)D, eps);
-      else if (nv <= 8)
-        rmsnorm_quant_warp_kernel<T, W, 8><<<grid, 256, 0, s>>>(xp0, wp0, q, scale, yp0, rows, (int)D, eps);
-      else
-        rmsnorm_quant_warp_kernel<T, W, 16><<<grid, 256, 0, s>>>(xp0, wp0, q, scale, yp0, rows, (int)D, eps);
-      return launch_status(cudaGetLastError());
-    }
     if (threads == 0) {
-      threads = nvec >= 512 ? 256 : (int)(((nvec + 31) / 32) * 32);
-      while ((nvec + threads - 1) / threads > 8 && threads < 1024) threads *= 2;
+      // about four 16-byte vectors per thread (measured best for D = 4096)
+      threads = (int)((((nvec + 3) / 4) + 31) / 32 * 32);
+      threads = threads < 32 ? 32 : (threads > 1024 ? 1024 : threads);
     }
     const int64_t nv = (nvec + threads - 1) / threads;
     if (nv > 8) return B200_ERR_UNSUPPORTED;

@@ -132,7 +132,6 @@ int b200_version(void) { return 100; }
 const char* b200_kernel_list(void) {
   return "rmsnorm_row_kernel\n"
          "rmsnorm_loop_kernel\n"
-         "rmsnorm_quant_warp_kernel\n"
          "rmsnorm_quant_row_kernel\n"
          "rope_kernel\n"
          "kv_scatter_kernel\n"
