@@ -505,7 +505,8 @@ def run_reference(args, ws, rank):
     }
 
 
-PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-skinny", "flash", "rmsnorm")
+PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-skinny", "flash", "rmsnorm", "rmsnorm-quant",
+                 "gemm-gelu", "append-prefill")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -533,6 +534,21 @@ def profile_case(name: str, reps: int = 3) -> None:
     elif name == "flash":
         q, k, v = WL.flash_inputs(B=1, H=8, T=4096, device=dev)
         fn = lambda: K.flash_attn(q, k, v, causal=True)  # noqa: E731
+    elif name == "rmsnorm-quant":
+        x, w = WL.rmsnorm_inputs(device=dev)
+        xb, wb = x.bfloat16().reshape(-1, 4096), w.bfloat16()
+        fn = lambda: K.rmsnorm_quant_int8(xb, wb)  # noqa: E731
+    elif name == "gemm-gelu":
+        g = torch.Generator(device=dev).manual_seed(11)
+        a_e = (torch.randn(2048, 4096, generator=g, device=dev) / 8).half()
+        b_e = torch.randn(4096, 4096, generator=g, device=dev).half()
+        bias_e = torch.randn(4096, generator=g, device=dev).half()
+        fn = lambda: K.gemm_bias_gelu(a_e, b_e, bias_e)  # noqa: E731
+    elif name == "append-prefill":
+        cache = WL.paged_cache(num_blocks=16384, block_size=BS, Hkv=HKV, D=D, device=dev, seed=9)
+        app = WL.decode_append_inputs(cache, n_tok=16384, Hq=HQ, device=dev, seed=9)
+        fn = lambda: K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"],  # noqa: E731
+                                            app["sin"], app["slot_mapping"], cache.k_cache, cache.v_cache)
     else:
         x, w = WL.rmsnorm_inputs(device=dev)
         fn = lambda: K.rmsnorm(x, w)  # noqa: E731

@@ -166,6 +166,20 @@ int b200_rope_kv_append_paged(const void* q, const void* k, const void* v,
                               int32_t dtype, int32_t cs_dtype,
                               const b200_launch_cfg* cfg, void* stream);
 
+/* Same, with a slot-ownership table for many new tokens (prefill): slot_owner
+ * is a caller buffer of owner_entries >= num_blocks * block_size int32,
+ * zero-filled before its first use and returned to zero by each call.  A
+ * later token writing the same slot wins, as in the reference's loop, in
+ * O(T) instead of a per-token scan of all later slots.  slot_owner NULL is
+ * b200_rope_kv_append_paged. */
+int b200_rope_kv_append_paged_ws(const void* q, const void* k, const void* v,
+                                 const int64_t* positions, const void* cos, const void* sin,
+                                 int64_t cs_rows, const int64_t* slot_mapping, void* q_out,
+                                 void* k_cache, void* v_cache, int64_t T, int64_t Hq,
+                                 int64_t Hkv, int64_t D, int64_t num_blocks, int64_t block_size,
+                                 int32_t dtype, int32_t cs_dtype, int32_t* slot_owner,
+                                 int64_t owner_entries, const b200_launch_cfg* cfg, void* stream);
+
 /* ---- paged attention decode -----------------------------------------------
  * Replaces triton_agent/ops/paged_attention/reference.py:10-54 (with the
  * query row indexed as q[b], and grouped-query attention: q head h reads kv

@@ -175,3 +175,21 @@ def test_fused_decode_append_edge_cases(dtype, cuda_device):
     sm[2] = 32 * 16                  # one past the end: skipped
     sm[5] = sm[3]                    # collision: token 5 wins
     _check_fused_append(cache, inp, cuda_device)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_append_prefill_slot_owner_table(dtype, cuda_device):
+    """More than 512 new tokens take the slot-ownership table path: later
+    tokens win collisions (including runs of three), invalid slots are
+    skipped, and a second call with another pattern sees a clean table."""
+    cache = WL.paged_cache(num_blocks=256, block_size=16, Hkv=2, D=128, dtype=dtype, device=cuda_device)
+    for seed in (0, 1):
+        inp = WL.decode_append_inputs(cache, n_tok=2000, Hq=4, max_pos=4096, device=cuda_device, seed=seed)
+        sm = inp["slot_mapping"]
+        sm[10] = -5
+        sm[11] = 256 * 16
+        sm[100] = sm[50]
+        sm[1500] = sm[50]              # three writers of one slot: token 1500 wins
+        sm[1999] = sm[0]
+        sm[7 + seed] = sm[900]         # token 900 wins over the earlier one
+        _check_fused_append(cache, inp, cuda_device)

@@ -89,6 +89,11 @@ SIGNATURES = {
         c_int,
         [P, P, P, P, P, P, I64_, P, P, P, P, I64_, I64_, I64_, I64_, I64_, I64_, c_int32, c_int32, PCFG, P],
     ),
+    "b200_rope_kv_append_paged_ws": (
+        c_int,
+        [P, P, P, P, P, P, I64_, P, P, P, P, I64_, I64_, I64_, I64_, I64_, I64_, c_int32, c_int32, P, I64_, PCFG,
+         P],
+    ),
     "b200_paged_attention_workspace_size": (c_size_t, [I64_, I64_, I64_, I64_, I64_, PCFG]),
     "b200_paged_attention": (
         c_int,

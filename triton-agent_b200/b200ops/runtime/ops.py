@@ -191,12 +191,19 @@ def rope_kv_append_paged(q, k, v, positions, cos, sin, slot_mapping, k_cache, v_
     if pos is not None and pos.dtype != torch.int64:
         raise L.B200OpsError(L.ERR_UNSUPPORTED, "rope_kv_append_paged", "positions must be int64")
     sm = _slots64(slot_mapping)
-    st = L.load().b200_rope_kv_append_paged(_ptr(q), _ptr(k), _ptr(v), _ptr(pos), _ptr(cos), _ptr(sin),
-                                            cos.shape[0], _ptr(sm), _ptr(q_out), _ptr(k_cache), _ptr(v_cache),
-                                            T, Hq, Hkv, D, nb, bs, dtype_code(k.dtype), dtype_code(cos.dtype),
-                                            _cfg(cfg), _stream(dev))
+    # many new tokens (prefill): slot-ownership table (zeroed once, restored by
+    # every call) instead of each token scanning all later slots
+    owner = WORKSPACES.get(dev, nb * bs * 4, "slot_owner") if T > OWNER_TABLE_MIN_TOKENS else None
+    st = L.load().b200_rope_kv_append_paged_ws(_ptr(q), _ptr(k), _ptr(v), _ptr(pos), _ptr(cos), _ptr(sin),
+                                               cos.shape[0], _ptr(sm), _ptr(q_out), _ptr(k_cache),
+                                               _ptr(v_cache), T, Hq, Hkv, D, nb, bs, dtype_code(k.dtype),
+                                               dtype_code(cos.dtype), _ptr(owner), nb * bs if owner is not None
+                                               else 0, _cfg(cfg), _stream(dev))
     L.check(st, "rope_kv_append_paged")
     return q_out
+
+
+OWNER_TABLE_MIN_TOKENS = 512
 
 
 # -------------------------------------------------------------- paged decode

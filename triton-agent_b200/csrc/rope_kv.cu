@@ -213,13 +213,27 @@ __device__ __forceinline__ void load_cs(const CS* p, float* out) {
   }
 }
 
+// Slot ownership for many new tokens (prefill): owner[slot] = 1 + the last
+// token writing it (atomic max; the reference's loop lets later tokens
+// overwrite earlier ones).  The append kernel then writes a token's K/V rows
+// only if it owns the slot, and the owner puts the entry back to 0, so the
+// zero-filled table is ready for the next call -- an O(n) replacement of
+// the per-token scan of all later slots (O(n^2) for a prefill).
+__global__ void slot_owner_kernel(const int64_t* __restrict__ slots, int64_t n_tok, int64_t slot_hi,
+                                  int* __restrict__ owner) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n_tok) return;
+  const int64_t slot = slots[t];
+  if (slot >= 0 && slot < slot_hi) atomicMax(&owner[slot], (int)(t + 1));
+}
+
 template <typename T, typename CS>
 __global__ void __launch_bounds__(1024) rope_kv_append_paged_fast_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const int64_t* __restrict__ positions, const CS* __restrict__ cos,
     const CS* __restrict__ sin, int64_t cs_rows, const int64_t* __restrict__ slots,
     T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t n_tok,
-    int Hq, int Hkv, int64_t D, int64_t slot_hi, int tpr) {
+    int Hq, int Hkv, int64_t D, int64_t slot_hi, int tpr, int* __restrict__ owner) {
   constexpr int VN = Vec<T>::N;
   const int64_t t = blockIdx.x;
   const int64_t half = D / 2;
@@ -240,9 +254,18 @@ __global__ void __launch_bounds__(1024) rope_kv_append_paged_fast_kernel(
     a = __ldg(reinterpret_cast<const uint4*>(src + c * VN));
     b = __ldg(reinterpret_cast<const uint4*>(src + half + c * VN));
   }
-  // collision scan: does a later token write the same slot?
+  // collision: does a later token write the same slot? (ownership table, or
+  // a scan of the later slots)
   int hit = 0;
-  for (int64_t j = t + 1 + threadIdx.x; j < n_tok; j += blockDim.x) hit |= (__ldg(&slots[j]) == slot);
+  if (owner != nullptr) {
+    if (threadIdx.x == 0 && slot >= 0 && slot < slot_hi) {
+      const int o = *(volatile int*)&owner[slot];
+      hit = o != (int)(t + 1);
+      if (!hit) owner[slot] = 0;  // back to zero for the next call (later readers are not owners)
+    }
+  } else {
+    for (int64_t j = t + 1 + threadIdx.x; j < n_tok; j += blockDim.x) hit |= (__ldg(&slots[j]) == slot);
+  }
   const bool pos_ok = pos >= 0 && pos < cs_rows;
   if (!pos_ok) pos = 0;
   float cv[VN], sv[VN];
@@ -451,7 +474,7 @@ int launch_fused(const void* q, const void* k, const void* v, const int64_t* pos
                  const void* cos, const void* sin, int64_t cs_rows, const int64_t* slots,
                  void* q_out, void* k_cache, void* v_cache, int64_t n_tok, int64_t Hq,
                  int64_t Hkv, int64_t D, int64_t slot_hi, const b200_launch_cfg* cfg,
-                 cudaStream_t s) {
+                 cudaStream_t s, int* owner) {
   constexpr int VN = Vec<T>::N;
   const int64_t half = D / 2;
   const void* ptrs[6] = {q, k, v, q_out, k_cache, v_cache};
@@ -474,8 +497,13 @@ int launch_fused(const void* q, const void* k, const void* v, const int64_t* pos
                       (VN * (int64_t)sizeof(CS)) % 16 == 0;
   if (vec && cs_vec && rows * tpr <= 1024 && !(cfg && cfg->threads > 0)) {
     const int th = (int)(((rows * tpr) + 31) / 32 * 32);
+    if (owner != nullptr) {
+      slot_owner_kernel<<<(unsigned)((n_tok + 255) / 256), 256, 0, s>>>(slots, n_tok, slot_hi, owner);
+      if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return launch_status(e);
+    }
     rope_kv_append_paged_fast_kernel<T, CS><<<(unsigned)n_tok, th, 0, s>>>(
-        qp, kp, vp, positions, cp, sp, cs_rows, slots, qo, kc, vc, n_tok, (int)Hq, (int)Hkv, D, slot_hi, tpr);
+        qp, kp, vp, positions, cp, sp, cs_rows, slots, qo, kc, vc, n_tok, (int)Hq, (int)Hkv, D, slot_hi, tpr,
+        owner);
     return launch_status(cudaGetLastError());
   }
   if (vec)
@@ -490,14 +518,13 @@ int launch_fused(const void* q, const void* k, const void* v, const int64_t* pos
 }
 }  // namespace
 
-extern "C" int b200_rope_kv_append_paged(const void* q, const void* k, const void* v,
-                                         const int64_t* positions, const void* cos,
-                                         const void* sin, int64_t cs_rows,
-                                         const int64_t* slot_mapping, void* q_out, void* k_cache,
-                                         void* v_cache, int64_t T, int64_t Hq, int64_t Hkv,
-                                         int64_t D, int64_t num_blocks, int64_t block_size,
-                                         int32_t dtype, int32_t cs_dtype,
-                                         const b200_launch_cfg* cfg, void* stream) {
+extern "C" int b200_rope_kv_append_paged_ws(const void* q, const void* k, const void* v,
+                                            const int64_t* positions, const void* cos, const void* sin,
+                                            int64_t cs_rows, const int64_t* slot_mapping, void* q_out,
+                                            void* k_cache, void* v_cache, int64_t T, int64_t Hq, int64_t Hkv,
+                                            int64_t D, int64_t num_blocks, int64_t block_size, int32_t dtype,
+                                            int32_t cs_dtype, int32_t* slot_owner, int64_t owner_entries,
+                                            const b200_launch_cfg* cfg, void* stream) {
   if (int e = injected_error("rope_kv_append_paged")) return e;
   if (T < 0 || Hkv <= 0 || D <= 0 || D % 2 != 0 || num_blocks <= 0 || block_size <= 0 ||
       cs_rows <= 0)
@@ -506,22 +533,37 @@ extern "C" int b200_rope_kv_append_paged(const void* q, const void* k, const voi
   if (q && Hq <= 0) return B200_ERR_BAD_ARG;
   if (T == 0) return B200_OK;
   if (!k || !v || !cos || !sin || !slot_mapping || !k_cache || !v_cache) return B200_ERR_BAD_ARG;
-  if (T > 0x7fffffffLL || Hq > 4096 || Hkv > 4096) return B200_ERR_UNSUPPORTED;
+  if (T > 0x7fffffffLL - 1 || Hq > 4096 || Hkv > 4096) return B200_ERR_UNSUPPORTED;
   const int64_t slot_hi = num_blocks * block_size;
+  if (slot_owner != nullptr && owner_entries < slot_hi) return B200_ERR_WORKSPACE;
+  int* owner = reinterpret_cast<int*>(slot_owner);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cs_dtype == dtype) {
     return B200_DISPATCH_FLOAT(dtype, [&] {
       return launch_fused<scalar_t, scalar_t>(q, k, v, positions, cos, sin, cs_rows, slot_mapping,
                                               q_out, k_cache, v_cache, T, Hq, Hkv, D, slot_hi,
-                                              cfg, s);
+                                              cfg, s, owner);
     });
   }
   if (cs_dtype == B200_F32) {
     return B200_DISPATCH_FLOAT(dtype, [&] {
       return launch_fused<scalar_t, float>(q, k, v, positions, cos, sin, cs_rows, slot_mapping,
                                            q_out, k_cache, v_cache, T, Hq, Hkv, D, slot_hi, cfg,
-                                           s);
+                                           s, owner);
     });
   }
   return B200_ERR_UNSUPPORTED;
+}
+
+extern "C" int b200_rope_kv_append_paged(const void* q, const void* k, const void* v,
+                                         const int64_t* positions, const void* cos,
+                                         const void* sin, int64_t cs_rows,
+                                         const int64_t* slot_mapping, void* q_out, void* k_cache,
+                                         void* v_cache, int64_t T, int64_t Hq, int64_t Hkv,
+                                         int64_t D, int64_t num_blocks, int64_t block_size,
+                                         int32_t dtype, int32_t cs_dtype,
+                                         const b200_launch_cfg* cfg, void* stream) {
+  return b200_rope_kv_append_paged_ws(q, k, v, positions, cos, sin, cs_rows, slot_mapping, q_out, k_cache,
+                                      v_cache, T, Hq, Hkv, D, num_blocks, block_size, dtype, cs_dtype, nullptr,
+                                      0, cfg, stream);
 }
