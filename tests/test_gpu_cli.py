@@ -49,12 +49,21 @@ def test_optimize_records_a_verified_best(strategy, tmp_path):
     res = CliRunner().invoke(cli.main, ["optimize", "rmsnorm", "--shape", "B=4,T=256,D=4096", "--dtype", "bf16",
                                         "--strategy", strategy, "--max-candidates", "4", "--out", str(tmp_path)])
     assert res.exit_code == 0, res.output
-    eps = list((tmp_path / "rmsnorm").glob("episode_*.json"))
+    eps = list((tmp_path / "rmsnorm").glob("*/record.json"))
     assert len(eps) == 1
     rec = json.loads(eps[0].read_text())
-    assert rec["best"]["result"]["verify_pass"] and rec["best"]["result"]["latency_us_p50"] > 0
-    assert len(rec["candidates"]) == 4
-    assert {c["action"]["threads"] for c in rec["candidates"]} <= {128, 256, 512, 1024}
+    assert rec["result"]["verify_pass"] and rec["result"]["latency_us_p50"] > 0
+    assert len(rec["extra"]["candidates"]) == 4
+    assert {c["action"]["threads"] for c in rec["extra"]["candidates"]} <= {128, 256, 512, 1024}
+    assert (tmp_path / "leaderboard.sqlite").exists()
+    # a second run warm-starts from the leaderboard's best and evaluates it first
+    res = CliRunner().invoke(cli.main, ["optimize", "rmsnorm", "--shape", "B=4,T=256,D=4096", "--dtype", "bf16",
+                                        "--strategy", strategy, "--max-candidates", "1", "--out", str(tmp_path)])
+    assert res.exit_code == 0, res.output
+    recs = sorted((tmp_path / "rmsnorm").glob("*/record.json"))
+    second = json.loads(recs[-1].read_text())
+    assert second["extra"]["warm_start"] and second["extra"]["candidates"][0]["action"] == \
+        second["extra"]["warm_start"][0]
 
 
 def test_bad_launch_config_becomes_a_failed_candidate():

@@ -3,6 +3,8 @@
     python -m b200ops.cli list
     python -m b200ops.cli verify-correctness OP [--shape K=V,...] [--dtype bf16]
     python -m b200ops.cli optimize OP [--shape ...] [--strategy grid|best_of_n|ucb|thompson|epsilon|reinforce|grpo]
+    python -m b200ops.cli leaderboard OP [--shape ...] [--dtype ...]
+    python -m b200ops.cli replay OP EPISODE_ID
 
 Pipeline glue follows the reference's triton_agent/cli.py: contracts are
 registered from ops/<op>/contract.yaml (:408-416), variants are discovered
@@ -193,6 +195,96 @@ def verify_correctness(op: str, shape: str, dtype: str, json_out: str | None) ->
         sys.exit(1)
 
 
+def shape_key(parsed: dict[str, int]) -> str:
+    """Leaderboard and config-store key of a --shape: its K=V pairs in key
+    order (the reference keys by "B=..,T=..,D=.." at cli.py:177; these
+    operators also have M/N/K, heads and cache axes)."""
+    return ",".join(f"{k}={parsed[k]}" for k in sorted(parsed)) or "default"
+
+
+def warm_start_actions(state: OpState, templates: dict[str, Any], config_store, leaderboard) -> list[tuple[str, OpAction]]:
+    """Historical best configurations for this (op, shape, dtype): the tuner's
+    ShapeConfigStore entry (microrl/trainer.py:41-80) and the leaderboard's
+    best row (core/storage.py:150-165), for variants that still exist,
+    without duplicates.  They are evaluated first, so a later search starts
+    from the best known launch configuration."""
+    found = []
+    hist = config_store.get_historical_best(state)
+    if hist:
+        found.append(OpAction.from_dict(hist))
+    row = leaderboard.best_config(state.op_name, state.shape, state.dtype)
+    if row:
+        found.append(leaderboard.action_of(row))
+    out, seen = [], set()
+    for a in found:
+        if a.template_id in templates and a.arm_key() not in seen:
+            seen.add(a.arm_key())
+            out.append((a.template_id, a))
+    return out
+
+
+def search(contract: OpContract, state: OpState, templates: dict[str, Any], eval_fn, strategy: str,
+           max_candidates: int, retry: int, store_path: Path, warm=()) -> tuple[list, list[CandidateResult]]:
+    """Candidate search of `optimize` (reference cli.py:57-160): grid or
+    best-of-n lists, or a bandit / policy-gradient / GRPO trainer choosing
+    one candidate per step, with repair-and-retry of failed candidates.
+    `warm` candidates are evaluated first.  eval_fn(template_id, action)
+    returns the CandidateResult."""
+    from .agent.generator import generate_best_of_n, generate_grid
+    from .agent.repairer import repair_action, should_retry
+    from .microrl.trainer import Trainer
+
+    warm = list(warm)
+    warm_keys = {a.arm_key() for _, a in warm}
+    if strategy in ("grid", "best_of_n"):
+        gen = generate_grid(contract, state, templates) if strategy == "grid" else \
+            generate_best_of_n(contract, state, templates, n=max_candidates, seed=0)
+        cands = (warm + [c for c in gen if c[1].arm_key() not in warm_keys])[:max_candidates]
+        return cands, [eval_fn(t, a) for t, a in cands]
+    all_c = warm + [c for c in generate_grid(contract, state, templates) if c[1].arm_key() not in warm_keys]
+    trainer = Trainer(strategy=strategy, store_path=store_path)
+    cands, results = [], []
+    for step in range(max_candidates):
+        i = step if step < len(warm) else trainer.select(all_c, state)
+        tid, action = all_c[i]
+        r = eval_fn(tid, action)
+        for _ in range(retry):
+            if r.compile_pass and r.verify_pass:
+                break
+            fixed = repair_action(action, r)
+            if not should_retry(fixed, action, r):
+                break
+            action = fixed
+            if all(a.arm_key() != action.arm_key() for _, a in all_c):
+                all_c.append((tid, action))
+            r = eval_fn(tid, action)
+        trainer.update(action, state, r, all_c)
+        cands.append((tid, action))
+        results.append(r)
+    return cands, results
+
+
+def record_outcome(state: OpState, cands: list, results: list[CandidateResult], best_i: int, out: Path,
+                   extra: dict[str, Any] | None = None) -> tuple[Path, str]:
+    """Saves the episode (core/storage.py:13-65 layout), upserts the best into
+    the leaderboard (storage.py:102-137, cli.py:171-181) and, when promoted,
+    into the ShapeConfigStore the next run warm-starts from."""
+    from .core.storage import EpisodeStore, LeaderboardStore
+    from .microrl.trainer import ShapeConfigStore
+
+    tid, action = cands[best_i]
+    best = results[best_i]
+    episode_id = f"{int(time.time() * 1000)}_{tid}"
+    rec_extra = dict(extra or {})
+    rec_extra["candidates"] = [{"action": a.to_dict(), "result": r.to_dict()} for (_, a), r in zip(cands, results)]
+    path = EpisodeStore(out).save(state.op_name, episode_id, state, action, best, extra=rec_extra)
+    LeaderboardStore(out / "leaderboard.sqlite").upsert(state.op_name, state.shape, state.dtype, state.device,
+                                                        action, best, episode_id)
+    if best.promoted:
+        ShapeConfigStore(out / "best_configs.json").set_best(state, action, best)
+    return path, episode_id
+
+
 @main.command()
 @click.argument("op")
 @click.option("--shape", default="")
@@ -201,20 +293,22 @@ def verify_correctness(op: str, shape: str, dtype: str, json_out: str | None) ->
               type=click.Choice(["grid", "best_of_n", "ucb", "thompson", "epsilon", "reinforce", "grpo"]))
 @click.option("--max-candidates", default=16, type=int)
 @click.option("--retry", default=1, type=int)
-@click.option("--out", default="episodes", help="directory for the episode record")
-def optimize(op: str, shape: str, dtype: str, strategy: str, max_candidates: int, retry: int, out: str) -> None:
+@click.option("--out", default="episodes", help="directory for episodes, leaderboard.sqlite and best_configs.json")
+@click.option("--warm-start/--no-warm-start", default=True, help="evaluate the stored best configuration first")
+def optimize(op: str, shape: str, dtype: str, strategy: str, max_candidates: int, retry: int, out: str,
+             warm_start: bool) -> None:
     """Searches the CUDA launch/tile space of OP and promotes the best variant."""
-    from .agent.generator import generate_best_of_n, generate_grid
     from .agent.promoter import should_promote
-    from .agent.repairer import repair_action, should_retry
     from .agent.selector import select_best
     from .core.profiler import time_device
-    from .microrl.trainer import Trainer
+    from .core.storage import LeaderboardStore
+    from .microrl.trainer import ShapeConfigStore
 
     ensure_registered(op)
     contract = get_registry().get(op)
     parsed = parse_shape(shape)
-    state = OpState(op, parsed.get("B", 8), parsed.get("T", 2048), parsed.get("D", 4096), dtype, "cuda")
+    state = OpState(op, parsed.get("B", 8), parsed.get("T", 2048), parsed.get("D", 4096), dtype, "cuda",
+                    shape=shape_key(parsed))
     templates = load_templates(op)
     ref_fn, gen_fn = load_reference(op)
     inputs = gen_fn(**parsed, dtype=_torch_dtype(dtype), device="cuda")
@@ -224,41 +318,55 @@ def optimize(op: str, shape: str, dtype: str, strategy: str, max_candidates: int
     baseline_us = lat[len(lat) // 2]
     state.baseline_latency_us = baseline_us
 
-    if strategy in ("grid", "best_of_n"):
-        cands = generate_grid(contract, state, templates) if strategy == "grid" else \
-            generate_best_of_n(contract, state, templates, n=max_candidates, seed=0)
-        cands = cands[:max_candidates]
-        results = [evaluate(op, contract, templates[t], a, state, inputs, ref_out, baseline_us) for t, a in cands]
-    else:
-        all_c = generate_grid(contract, state, templates)
-        trainer = Trainer(strategy=strategy, store_path=Path(out) / "best_configs.json")
-        cands, results = [], []
-        for _ in range(max_candidates):
-            i = trainer.select(all_c, state)
-            tid, action = all_c[i]
-            r = evaluate(op, contract, templates[tid], action, state, inputs, ref_out, baseline_us)
-            for _ in range(retry):
-                if r.compile_pass and r.verify_pass:
-                    break
-                fixed = repair_action(action, r)
-                if not should_retry(fixed, action, r):
-                    break
-                action = fixed
-                r = evaluate(op, contract, templates[tid], action, state, inputs, ref_out, baseline_us)
-            trainer.update(action, state, r, all_c)
-            cands.append((tid, action))
-            results.append(r)
+    outdir = Path(out)
+    warm = warm_start_actions(state, templates, ShapeConfigStore(outdir / "best_configs.json"),
+                              LeaderboardStore(outdir / "leaderboard.sqlite")) if warm_start else []
+    cands, results = search(contract, state, templates,
+                            lambda t, a: evaluate(op, contract, templates[t], a, state, inputs, ref_out, baseline_us),
+                            strategy, max_candidates, retry, outdir / "best_configs.json", warm)
     best_i, best = select_best(cands, results)
     best.promoted = should_promote(best, contract)
-    record = {"op": op, "shape": parsed, "dtype": dtype, "strategy": strategy, "baseline_latency_us": baseline_us,
-              "time": time.time(), "best": {"action": cands[best_i][1].to_dict(), "result": best.to_dict()},
-              "candidates": [{"action": a.to_dict(), "result": r.to_dict()} for (_, a), r in zip(cands, results)]}
-    outdir = Path(out) / op
-    outdir.mkdir(parents=True, exist_ok=True)
-    path = outdir / f"episode_{int(time.time())}.json"
-    path.write_text(json.dumps(record, indent=2))
+    path, _ = record_outcome(state, cands, results, best_i, outdir,
+                             {"strategy": strategy, "shape": parsed, "baseline_latency_us": baseline_us,
+                              "warm_start": [a.to_dict() for _, a in warm]})
     click.echo(f"best {cands[best_i][0]} {cands[best_i][1].launch_cfg()} p50={best.latency_us_p50:.1f}us "
                f"speedup={best.speedup:.2f}x reward={best.reward:.2f} promoted={best.promoted} -> {path}")
+
+
+@main.command("leaderboard")
+@click.argument("op")
+@click.option("--shape", default="", help="only this shape (K=V,... as given to optimize)")
+@click.option("--dtype", default="")
+@click.option("--out", default="episodes")
+@click.option("--limit", default=20, type=int)
+def leaderboard(op: str, shape: str, dtype: str, out: str, limit: int) -> None:
+    """Best recorded configurations of OP (reference cli.py:419-467)."""
+    from .core.storage import LeaderboardStore
+
+    key = shape_key(parse_shape(shape)) if shape else None
+    rows = LeaderboardStore(Path(out) / "leaderboard.sqlite").query(op, shape=key, dtype=dtype or None, limit=limit)
+    if not rows:
+        click.echo(f"no entries for {op}")
+        return
+    for r in rows:
+        click.echo(f"{r['shape']} {r['dtype']} {r['template_id']} threads={r['threads']} split={r['split']} "
+                   f"tile={r['tile_m']}x{r['tile_n']}x{r['tile_k']} stages={r['num_stages']} "
+                   f"p50={r['latency_us_p50']:.1f}us speedup={r['speedup']:.2f}x "
+                   f"roofline={r['roofline_fraction']:.2f} promoted={bool(r['promoted'])} ep={r['episode_id']}")
+
+
+@main.command("replay")
+@click.argument("op")
+@click.argument("episode_id")
+@click.option("--out", default="episodes")
+def replay(op: str, episode_id: str, out: str) -> None:
+    """Prints a stored episode record (reference cli.py:470-490)."""
+    from .core.storage import EpisodeStore
+
+    rec = EpisodeStore(out).load(op, episode_id)
+    if rec is None:
+        raise click.ClickException(f"episode {op}/{episode_id} not found")
+    click.echo(json.dumps({k: rec[k] for k in ("episode_id", "state", "action", "result")}, indent=2))
 
 
 if __name__ == "__main__":

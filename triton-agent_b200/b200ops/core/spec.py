@@ -23,6 +23,9 @@ class OpState:
     gpu_name: str = ""
     baseline_latency_us: float = 0.0
     historical_best_config: dict | None = None
+    # the generator's full shape ("K=V,..." in key order) for operators whose
+    # shape is not B/T/D (GEMM M,N,K; paged caches; heads); empty = B/T/D only
+    shape: str = ""
 
     def to_dict(self) -> dict[str, Any]:
         return asdict(self)
@@ -32,7 +35,7 @@ class OpState:
         req = {k: data[k] for k in ("op_name", "B", "T", "D", "dtype", "device")}
         return cls(**req, gpu_name=data.get("gpu_name", ""),
                    baseline_latency_us=data.get("baseline_latency_us", 0.0),
-                   historical_best_config=data.get("historical_best_config"))
+                   historical_best_config=data.get("historical_best_config"), shape=data.get("shape", ""))
 
 
 CUDA_FIELDS = ("threads", "rows_per_cta", "split", "tile_m", "tile_n", "tile_k")

@@ -20,6 +20,10 @@ from ..core.spec import OpAction, OpState
 
 
 def context_key(state: OpState) -> str:
+    """(op, shape, dtype, device) key of bandit arms and stored best configs
+    (microrl/trainer.py:59-60); the full generator shape when the state has one."""
+    if state.shape:
+        return f"{state.op_name}|{state.shape}|{state.dtype}|{state.device}"
     return f"{state.op_name}|{state.B}|{state.T}|{state.D}|{state.dtype}|{state.device}"
 
 
