@@ -129,3 +129,29 @@ def test_generic_path_head_dim_64(cuda_device):
     cache = WL.paged_cache(num_blocks=64, block_size=16, Hkv=4, D=64, device=cuda_device, seed=9)
     inp = WL.decode_attention_inputs(cache, B=3, Hq=12, ctx_lo=3, ctx_hi=300, device=cuda_device, seed=9)
     run_and_check(inp["q"], cache.k_cache, cache.v_cache, inp["block_table"], inp["context_len"], cuda_device)
+
+
+# Persistent kernel partitions: equal static ranges only (flags 4), and
+# static ranges plus claimed chunks of tile_n pages for tile_k percent of the
+# entries, on grids of tile_m CTAs.  Ranges are a fixed partition of the
+# entries, so results must not depend on which CTA claimed which chunk.
+@pytest.mark.parametrize("cfg", [{"flags": 4}, {}, {"tile_k": 25}, {"tile_n": 1, "tile_k": 50}, {"tile_n": 2, "tile_k": 90},
+                                 {"tile_m": 16, "tile_n": 1, "tile_k": 60}, {"tile_m": 3, "tile_k": 30},
+                                 {"rows_per_cta": 4, "tile_k": 40, "tile_n": 3}])
+def test_persistent_claimed_chunks(cfg, cuda_device):
+    cache = WL.paged_cache(num_blocks=2048, block_size=16, Hkv=8, D=128, device=cuda_device, seed=21)
+    inp = WL.decode_attention_inputs(cache, B=16, Hq=32, ctx_lo=1, ctx_hi=1500, device=cuda_device, seed=21)
+    bt, cl = inp["block_table"].clone(), inp["context_len"]
+    bt[3, 2] = -1  # dropped entry inside a claimed range shifts later blocks
+    outs = [run_and_check(inp["q"], cache.k_cache, cache.v_cache, bt, cl, cuda_device, cfg=cfg) for _ in range(2)]
+    assert torch.equal(outs[0], outs[1])  # the claim counter re-armed itself; same partition, same bits
+    # edge contexts (0, 1, page boundaries) with dropped ids, few entries
+    cache2 = WL.paged_cache(num_blocks=128, block_size=16, Hkv=8, D=128, device=cuda_device, seed=3)
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    bt2 = torch.randint(0, 128, (9, 20), generator=g, device=cuda_device).to(torch.int32)
+    cl2 = torch.tensor([1, 15, 16, 17, 32, 0, 319, 320, 200], device=cuda_device, dtype=torch.int32)
+    bt2[6, 3] = -1
+    bt2[8, 0] = 128
+    q2 = torch.randn(9, 32, 128, generator=g, device=cuda_device).bfloat16()
+    out2 = run_and_check(q2, cache2.k_cache, cache2.v_cache, bt2, cl2, cuda_device, cfg=cfg)
+    assert torch.count_nonzero(out2[5]) == 0

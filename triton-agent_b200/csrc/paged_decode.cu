@@ -24,6 +24,7 @@
 //   When a sequence spans several splits, each CTA writes (m, l, o) to the
 //   workspace and the last CTA to finish (atomic ticket) merges them and
 //   resets the ticket, so one launch does the whole op.
+#include <limits.h>
 #include <math.h>
 #include <stdio.h>
 
@@ -86,19 +87,27 @@ __device__ __forceinline__ bool bad_block(IDX id, int64_t nb) {
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core consumer (block size a multiple of 16).  Warp w owns kv head
-// h0 + w; its G query heads are rows 0..G-1 of a 16-row mma.sync tile (the
-// other rows are zero).  Per 16-token chunk of a page:
-//   S[16 x 16 tok] = Q[16 x 128] K^T   -- 8 k-steps x 2 n-tiles of m16n8k16,
-//                                         K fragments by ldmatrix (rows = tokens)
-//   online softmax on the C fragments: each thread holds 4 scores of head
-//   lane/4 (tokens 2(lane%4)+{0,1}, +8); the row max needs 2 xor-shuffles
-//   O[16 x 128] += P[16 x 16] V       -- P reused from the S fragments as the A
-//                                         operand, V fragments by ldmatrix.trans
-// Shared-memory tiles are SWIZZLE_128B with rows = (head, token), so the 8
-// rows of every ldmatrix matrix hit 8 distinct 16-byte bank groups.  The
-// running max is raised only when it grows by more than 2^8 (exact: O and
-// l share the offset).
+// Tensor-core consumer (block size a multiple of 16), transposed form.  Warp
+// w owns kv head h0 + w and its G query heads.  Tokens are the M dimension of
+// the m16n8k16 tiles and query heads the N dimension (8 columns, heads >= G
+// are zero), so a 16-token chunk of a page costs 8 + 8 mma.sync:
+//   S^T[16 tok x 8 heads] = K[16 x 128] Q^T  -- 8 k-steps, K as the A operand
+//                                              by ldmatrix (rows = tokens), two
+//                                              independent accumulator chains
+//   online softmax on the C fragments: a thread holds tokens lane/4 and
+//   lane/4 + 8 of heads 2(lane%4) and 2(lane%4)+1; a head's max over the 16
+//   tokens needs 3 xor-shuffles
+//   O^T[128 x 8 heads] += V^T[128 x 16 tok] P^T  -- 8 m-tiles of 16 dims, V as
+//                                              the A operand by ldmatrix.trans;
+//                                              P^T's B fragments are the packed
+//                                              S^T fragments transposed in
+//                                              registers by movmatrix
+// The accumulator is 8 tiles x 4 floats per thread, and the V fragments are
+// loaded before the softmax so their latency overlaps it.  Shared-memory
+// tiles are SWIZZLE_128B with rows = (head, token), so the 8 rows of every
+// ldmatrix matrix hit 8 distinct 16-byte bank groups.  Each head's running
+// max is raised only when it grows by more than 2^8 (exact: O and l share the
+// offset).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -110,22 +119,29 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+// 8x8 b16 matrix transpose across the warp (fragment layout: row lane/4,
+// columns 2(lane%4) and 2(lane%4)+1 in one register).
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
 
 template <typename T>
-__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  // A rows 8..15 are zero (a1, a3 = 0)
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   } else {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 }
 
@@ -140,91 +156,173 @@ __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   }
 }
 
-// Zeroes the 16-bit halves of a B fragment register whose token is >= ntok.
+// Zeroes the 16-bit halves of a fragment register whose token is >= ntok.
 __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int ntok) {
   const uint32_t lo = tok < ntok ? 0x0000ffffu : 0u;
   const uint32_t hi = tok + 1 < ntok ? 0xffff0000u : 0u;
   return v & (lo | hi);
 }
 
+// Q^T B fragments of this warp's query heads: head lane/4 (zero if >= G),
+// dims 16ks + 2(lane%4) + {0,1} and +8.
+template <typename T, int G>
+__device__ __forceinline__ void load_q_frags(const T* __restrict__ qrow0, int lane, uint32_t (&qb)[8][2]) {
+  const int qh = lane >> 2, qc = (lane & 3) * 2;
+  const T* qr = qrow0 + (qh < G ? qh : 0) * kD;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    qb[ks][0] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + qc) : 0u;
+    qb[ks][1] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + qc) : 0u;
+  }
+}
+
+// Raises head c's running max to mx when it grew by more than 2^8; o entries
+// of that head are columns c and c + 2 of every tile.
+__device__ __forceinline__ void raise_max(float& mu, float mx, float& lp, float (&o)[8][4], int c) {
+  if (mu == -INFINITY) {
+    mu = mx;
+  } else if (mx > mu + 8.0f) {
+    const float alpha = exp2f(mu - mx);
+    mu = mx;
+    lp *= alpha;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      o[mt][c] *= alpha;
+      o[mt][c + 2] *= alpha;
+    }
+  }
+}
+
 // One page (ntok tokens of one kv head, K tile at kb, V tile at vb in the
-// swizzled [d-half][head][token][64] layout) folded into the running
-// (o, m_used, l_part) of this warp's query heads.
+// swizzled [d-half][head][token][64] layout) folded into this warp's running
+// (o, mu, lp): mu/lp[0] for head 2(lane%4), [1] for head 2(lane%4)+1.
 template <typename T>
 __device__ __forceinline__ void mma_page(uint32_t kb, uint32_t vb, int ntok, int w, int bs, int lane,
-                                         uint32_t hbytes, float sl2, const uint32_t (&qa)[8][2],
-                                         float (&o)[16][4], float& m_used, float& l_part) {
-  const int qc = (lane & 3) * 2;
+                                         uint32_t hbytes, float sl2, const uint32_t (&qb)[8][2],
+                                         float (&o)[8][4], float (&mu)[2], float (&lp)[2]) {
   const int mat = lane >> 3, mrow = lane & 7;
+  const int tr = lane >> 2, tq = (lane & 3) * 2;
   for (int t0 = 0; t0 < ntok; t0 += 16) {
-    float sc[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
     {
-      // lane supplies row `mrow` of matrix `mat`: (n-tile mat>>1, d-chunk parity mat&1)
-      const int row = w * bs + t0 + (mat >> 1) * 8 + mrow;
+      // A = K rows: matrix `mat` = (token half mat&1, dim-chunk parity mat>>1)
+      const int row = w * bs + t0 + (mat & 1) * 8 + mrow;
       const uint32_t rbase = kb + row * 128;
       const int sw = row & 7;
+      uint32_t ka[8][4];
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        const int chunk = ((ks & 3) << 1) | (mat & 1);
-        uint32_t b00, b01, b10, b11;
-        ldsm_x4(rbase + (ks >> 2) * hbytes + ((chunk ^ sw) << 4), b00, b01, b10, b11);
-        mma16816<T>(sc[0], qa[ks][0], qa[ks][1], b00, b01);
-        mma16816<T>(sc[1], qa[ks][0], qa[ks][1], b10, b11);
+        const int chunk = ((ks & 3) << 1) | (mat >> 1);
+        ldsm_x4(rbase + (ks >> 2) * hbytes + ((chunk ^ sw) << 4), ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3]);
       }
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        mma16816<T>((ks & 1) ? s1 : s0, ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3], qb[ks][0], qb[ks][1]);
     }
-    float x[4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = t0 + nt * 8 + qc + e;
-        x[nt * 2 + e] = tok < ntok ? sc[nt][e] * sl2 : -INFINITY;
-      }
-    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    if (m_used == -INFINITY) {
-      m_used = mx;
-    } else if (mx > m_used + 8.0f) {
-      const float alpha = exp2f(m_used - mx);
-      m_used = mx;
-      l_part *= alpha;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        o[j][0] *= alpha;
-        o[j][1] *= alpha;
-      }
-    }
-    float pv[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      pv[j] = exp2f(x[j] - m_used);
-      l_part += pv[j];
-    }
-    const uint32_t pa0 = pack_pair<T>(pv[0], pv[1]);  // tokens qc+{0,1}
-    const uint32_t pa2 = pack_pair<T>(pv[2], pv[3]);  // tokens 8+qc+{0,1}
-    const bool partial = (t0 + 16 > ntok);
+    // A = V^T by ldmatrix.trans: matrix `mat` = (token half mat>>1, dim-chunk parity mat&1)
+    uint32_t va[8][4];
     {
-      // matrix `mat`: token half mat&1, d-chunk offset mat>>1
-      const int row = w * bs + t0 + (mat & 1) * 8 + mrow;
+      const int row = w * bs + t0 + (mat >> 1) * 8 + mrow;
       const uint32_t rbase = vb + row * 128;
       const int sw = row & 7;
 #pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        const int d0 = np * 16 + (mat >> 1) * 8;
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(rbase + (d0 >> 6) * hbytes + ((((d0 & 63) >> 3) ^ sw) << 4), v0, v1, v2, v3);
-        if (partial) {
-          v0 = mask_pair(v0, t0 + qc, ntok);
-          v1 = mask_pair(v1, t0 + 8 + qc, ntok);
-          v2 = mask_pair(v2, t0 + qc, ntok);
-          v3 = mask_pair(v3, t0 + 8 + qc, ntok);
-        }
-        mma16816<T>(o[2 * np], pa0, pa2, v0, v1);
-        mma16816<T>(o[2 * np + 1], pa0, pa2, v2, v3);
+      for (int mt = 0; mt < 8; ++mt) {
+        const int chunk = ((mt & 3) << 1) | (mat & 1);
+        ldsm_x4_t(rbase + (mt >> 2) * hbytes + ((chunk ^ sw) << 4), va[mt][0], va[mt][1], va[mt][2], va[mt][3]);
       }
+    }
+    // x[0]/x[1]: token tr of heads 2(lane%4), +1; x[2]/x[3]: token tr + 8
+    const bool ok0 = t0 + tr < ntok, ok1 = t0 + tr + 8 < ntok;
+    float x[4];
+    x[0] = ok0 ? (s0[0] + s1[0]) * sl2 : -INFINITY;
+    x[1] = ok0 ? (s0[1] + s1[1]) * sl2 : -INFINITY;
+    x[2] = ok1 ? (s0[2] + s1[2]) * sl2 : -INFINITY;
+    x[3] = ok1 ? (s0[3] + s1[3]) * sl2 : -INFINITY;
+    float mA = fmaxf(x[0], x[2]), mB = fmaxf(x[1], x[3]);
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, off));
+      mB = fmaxf(mB, __shfl_xor_sync(0xffffffffu, mB, off));
+    }
+    raise_max(mu[0], mA, lp[0], o, 0);
+    raise_max(mu[1], mB, lp[1], o, 1);
+    const float p0 = exp2f(x[0] - mu[0]), p2 = exp2f(x[2] - mu[0]);
+    const float p1 = exp2f(x[1] - mu[1]), p3 = exp2f(x[3] - mu[1]);
+    lp[0] += p0 + p2;
+    lp[1] += p1 + p3;
+    // P^T B fragments: tokens tq + {0,1} (b0) and 8 + tq + {0,1} (b1) of head lane/4
+    const uint32_t b0 = movm_t(pack_pair<T>(p0, p1));
+    const uint32_t b1 = movm_t(pack_pair<T>(p2, p3));
+    if (t0 + 16 > ntok) {
+      // tokens past the end may hold anything (NaN included): zero their V
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        va[mt][0] = mask_pair(va[mt][0], t0 + tq, ntok);
+        va[mt][1] = mask_pair(va[mt][1], t0 + tq, ntok);
+        va[mt][2] = mask_pair(va[mt][2], t0 + 8 + tq, ntok);
+        va[mt][3] = mask_pair(va[mt][3], t0 + 8 + tq, ntok);
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) mma16816<T>(o[mt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], b0, b1);
+  }
+}
+
+// Sum of a head's l over the 8 lanes that share it.
+__device__ __forceinline__ float head_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 16);
+  return v;
+}
+
+// Normalised output rows of this warp's heads: orow0 = row of head 0; the
+// O^T fragments are transposed back by movmatrix into 4-byte stores of two
+// dims of head lane/4.
+template <typename T, int G>
+__device__ __forceinline__ void store_rows(T* __restrict__ orow0, const float (&o)[8][4], float lA, float lB,
+                                           int lane) {
+  const float iA = lA > 0.f ? 1.f / lA : 0.f, iB = lB > 0.f ? 1.f / lB : 0.f;
+  const int h = lane >> 2, tq = (lane & 3) * 2;
+  T* orow = orow0 + (h < G ? h : 0) * kD;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const uint32_t r0 = movm_t(pack_pair<T>(o[mt][0] * iA, o[mt][1] * iB));
+    const uint32_t r1 = movm_t(pack_pair<T>(o[mt][2] * iA, o[mt][3] * iB));
+    if (h < G) {
+      *reinterpret_cast<uint32_t*>(orow + 16 * mt + tq) = r0;
+      *reinterpret_cast<uint32_t*>(orow + 16 * mt + 8 + tq) = r1;
+    }
+  }
+}
+
+// Unnormalised fp32 partial of this warp's heads: row(h) = base + h * pitch
+// floats holds o[0..127]; (m, l) go to mpos(h), mpos(h) + 1 via ml_base +
+// h * ml_pitch.
+template <int G>
+__device__ __forceinline__ void store_partial(float* __restrict__ base, int64_t pitch, float* __restrict__ ml_base,
+                                              int64_t ml_pitch, const float (&o)[8][4], const float (&mu)[2],
+                                              float lA, float lB, int lane) {
+  const int hA = (lane & 3) * 2, hB = hA + 1, d = lane >> 2;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    if (hA < G) {
+      base[hA * pitch + 16 * mt + d] = o[mt][0];
+      base[hA * pitch + 16 * mt + 8 + d] = o[mt][2];
+    }
+    if (hB < G) {
+      base[hB * pitch + 16 * mt + d] = o[mt][1];
+      base[hB * pitch + 16 * mt + 8 + d] = o[mt][3];
+    }
+  }
+  if (d == 0) {
+    if (hA < G) {
+      ml_base[hA * ml_pitch] = mu[0];
+      ml_base[hA * ml_pitch + 1] = lA;
+    }
+    if (hB < G) {
+      ml_base[hB * ml_pitch] = mu[1];
+      ml_base[hB * ml_pitch + 1] = lB;
     }
   }
 }
@@ -238,22 +336,12 @@ __device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, u
   const int HG = p.HG;
   const int bs = (int)p.block_size;
   const int64_t kvh = (int64_t)hg * HG + w;
-  const int qh = lane >> 2;        // query head row of this thread (valid if < G)
-  const int qc = (lane & 3) * 2;   // column pair inside an 8-wide n-tile
-  // Q fragments (A operand), rows >= G are zero.
-  uint32_t qa[8][2];
-  {
-    const T* qr = q + (b * p.Hq + kvh * G + (qh < G ? qh : 0)) * kD;
+  uint32_t qb[8][2];
+  load_q_frags<T, G>(q + (b * p.Hq + kvh * G) * kD, lane, qb);
+  float o[8][4];
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      qa[ks][0] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + qc) : 0u;
-      qa[ks][1] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + qc) : 0u;
-    }
-  }
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_used = -INFINITY, l_part = 0.f;
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mu[2] = {-INFINITY, -INFINITY}, lp[2] = {0.f, 0.f};
   const float sl2 = p.qscale;
   const uint32_t base = sm100::smem_u32(smem);
   const uint32_t hbytes = p.stage_bytes / 4;
@@ -269,32 +357,19 @@ __device__ __forceinline__ void consume_mma(uint8_t* smem, uint64_t* full_bar, u
     const int ntok = list_ntok[i];
     const uint32_t kb = base + s * p.stage_bytes;
     const uint32_t vb = kb + 2 * hbytes;
-    mma_page<T>(kb, vb, ntok, w, bs, lane, hbytes, sl2, qa, o, m_used, l_part);
+    mma_page<T>(kb, vb, ntok, w, bs, lane, hbytes, sl2, qb, o, mu, lp);
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&empty_bar[s]));
   }
 
-  float l = l_part;
-  l += __shfl_xor_sync(0xffffffffu, l, 1);
-  l += __shfl_xor_sync(0xffffffffu, l, 2);
-  if (qh >= G) return;
-  const int64_t qrow = b * p.Hq + kvh * G + qh;
+  const float lA = head_sum(lp[0]), lB = head_sum(lp[1]);
+  const int64_t qrow0 = b * p.Hq + kvh * G;
   if (nsplit == 1) {
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    T* orow = out + qrow * kD;
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      *reinterpret_cast<uint32_t*>(orow + 8 * j + qc) = pack_pair<T>(o[j][0] * inv, o[j][1] * inv);
+    store_rows<T, G>(out + qrow0 * kD, o, lA, lB, lane);
   } else {
     const int heads_cta = HG * G;
-    const int64_t prow = ((b * p.n_hg + hg) * (int64_t)p.max_splits + split) * heads_cta + w * G + qh;
-    float* po = ws_o + prow * kD;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) *reinterpret_cast<float2*>(po + 8 * j + qc) = make_float2(o[j][0], o[j][1]);
-    if ((lane & 3) == 0) {
-      ws_ml[prow * 2] = m_used;
-      ws_ml[prow * 2 + 1] = l;
-    }
+    const int64_t prow = ((b * p.n_hg + hg) * (int64_t)p.max_splits + split) * heads_cta + w * G;
+    store_partial<G>(ws_o + prow * kD, kD, ws_ml + prow * 2, 2, o, mu, lA, lB, lane);
     __threadfence();
   }
 }
@@ -726,42 +801,89 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(
 // Persistent flat-partition decode (tensor-core consumer).
 //
 // All sequences' block-table entries are laid end to end (segment s = hg*B + b
-// holds ceil(ctx_b / bs) entries) and the grid's CTAs -- one per SM -- take
-// equal contiguous ranges of that list, so every SM streams the same number
-// of KV pages whatever the context lengths are.  The producer warp walks its
-// range segment by segment without draining the TMA ring: each stage carries
-// a small PageMeta record, either a data page (ntok surviving tokens) or an
-// end-of-segment marker.  On a marker the consumer warps finish the segment:
-// a segment wholly inside this CTA's range is written directly; otherwise the
-// CTA writes its (m, l, o) piece to one of its two partial slots (slot 0 for
-// the first segment of its range, 1 for the last) and the CTA that finishes
-// the segment's last piece (atomic ticket) merges the pieces.  Per segment,
-// the token rank rule of the reference (dropped ids shift later blocks) is
-// applied exactly as in the split kernel.
+// holds ceil(ctx_b / bs) entries) and cut into ranges: the first E - D entries
+// into one equal contiguous range per CTA (one CTA per SM), the last D
+// entries (dyn_pct percent of E) into chunks of `chunk` entries that CTAs
+// claim from an atomic counter once their own range is streamed, which evens
+// out finish times when SMs stream at different rates (off by default: see
+// kFlatDynPct).  The producer warp walks each range segment by segment
+// without draining the TMA ring: each stage carries a small PageMeta record,
+// either a data page (ntok surviving tokens) or an end-of-segment marker.
+// On a marker the consumer warps finish the segment: a segment wholly inside one range is
+// written directly; otherwise the CTA writes its (m, l, o) piece to one of
+// the range's two partial slots (slot 0 for the first segment of the range,
+// 1 for the last) and the CTA that finishes the segment's last piece (atomic
+// ticket) merges the pieces: per-head max and 1/sum first, then per-piece
+// weights in shared memory and independent 16-byte loads of the pieces' o
+// rows (a loop of dependent loads per element held the merging CTA's stream
+// for ~25 us and set the kernel's tail: 209 us against 193 us now).  The claim counter resets itself: the last CTA
+// to find the pool empty zeroes it.  Per segment, the token rank rule of the
+// reference (dropped ids shift later blocks) is applied exactly as in the
+// split kernel.
 // ---------------------------------------------------------------------------
 constexpr int kFlatMaxSeg = 1024;
+constexpr int kFlatPitch = kD + 4;  // floats per partial row: o[128], m, l, pad (16-byte rows)
+// Default share of entries handed out as claimed chunks: 0.  With the bench
+// shape (64 sequences, 148 CTAs) claimed chunks of 4-8 pages make tens of
+// pieces per sequence and the merges cost more than the balancing gains
+// (measured 262-334 us vs 193 us for equal ranges); cfg tile_k turns them on.
+constexpr int kFlatDynPct = 0;
+constexpr int kFlatChunk = 4;    // default entries (pages) per claimed chunk
+
+// Partial (m, l, o) rows of the persistent kernel: two per range, ranges =
+// static ones (<= grid) + claimed chunks.
+constexpr int kFlatChunksPerCta = 8;  // at most this many claimed chunks per CTA of the grid
+__host__ __device__ inline int64_t flat_partial_rows(int64_t grid, int64_t entries_max, int dyn_pct, int chunk,
+                                                     int64_t heads_cta) {
+  const int64_t dyn = entries_max * dyn_pct / 100 + 1;
+  int64_t nch = (dyn + chunk - 1) / chunk;
+  if (nch > kFlatChunksPerCta * grid) nch = kFlatChunksPerCta * grid;
+  return 2 * (grid + nch + 1) * heads_cta;
+}
 
 struct FlatParams {
   int64_t B, Hq, Hkv, num_blocks, block_size, max_blocks;
   int HG, n_hg, stages, nseg;
+  int dyn_pct;  // share of the entries handed out as claimed chunks (0..90)
+  int chunk;    // entries per claimed chunk (raised so that there are at most max_chunks)
+  int max_chunks;
   uint32_t stage_bytes;
   float qscale;
 };
+
+// Claim counters of the persistent kernel: the last two ints of the ticket
+// region ([0] next chunk, [1] CTAs done).
+constexpr int kPoolInts = 2;
 
 struct PageMeta {
   int kind;     // 0 data page, 1 end of segment, 2 end of stream
   int ntok;     // data: surviving tokens of the page
   int seg;      // segment id hg * B + b
-  int slot;     // marker: partial slot of this CTA's piece, or -1 when direct
-  int c1, c2;   // marker: CTAs holding the segment's pieces
-  int c1_slot;  // marker: slot used by the piece of CTA c1
-  int pad;
+  int slot;     // marker: partial slot of this range's piece, or -1 when direct
+  int c1, c2;   // marker: ranges holding the segment's pieces
+  int c1_slot;  // marker: slot used by the piece of range c1
+  int rng;      // marker: range id of this piece
 };
 
 __device__ __forceinline__ int64_t flat_lo(int64_t c, int64_t E, int64_t G) { return c * E / G; }
 __device__ __forceinline__ int flat_owner(int64_t e, int64_t E, int64_t G) {
   return (int)(((e + 1) * G + E - 1) / E - 1);
 }
+
+// Ranges of the entry list: Gs equal static ranges over [0, S), then chunks
+// of CH entries over [S, E).
+struct FlatRanges {
+  int64_t S, E, Gs;
+  int64_t CH;
+  __device__ __forceinline__ int64_t lo(int64_t r) const {
+    if (r <= Gs) return Gs > 0 ? flat_lo(r, S, Gs) : 0;
+    const int64_t x = S + (r - Gs) * CH;
+    return x < E ? x : E;
+  }
+  __device__ __forceinline__ int of(int64_t e) const {
+    return e < S ? flat_owner(e, S, Gs) : (int)(Gs + (e - S) / CH);
+  }
+};
 
 template <typename T, typename IDX, int G>
 __global__ void __launch_bounds__(288, 1)
@@ -786,6 +908,7 @@ __global__ void __launch_bounds__(288, 1)
   int* chunk_ntok = chunk_id + 32;
   float* s_comb = reinterpret_cast<float*>(chunk_ntok + 32);  // [2][64]
   int* s_flags = reinterpret_cast<int*>(s_comb + 128);        // [0] abort, [1] last piece
+  float* s_w = reinterpret_cast<float*>(s_flags + 4);         // merge weights [heads_cta][32]
 
   // ---- prologue: contexts, entry prefix over segments, barriers
   if (warp == HG) {
@@ -825,7 +948,15 @@ __global__ void __launch_bounds__(288, 1)
   __syncthreads();
   const int64_t E = s_cum[p.nseg];
   const int64_t Gc = gridDim.x;
-  const int64_t Geff = E < Gc ? E : Gc;
+  FlatRanges R;
+  R.E = E;
+  R.S = E - E * p.dyn_pct / 100;
+  R.Gs = R.S < Gc ? R.S : Gc;
+  R.CH = p.chunk;
+  if (R.CH * p.max_chunks < E - R.S) R.CH = (E - R.S + p.max_chunks - 1) / p.max_chunks;
+  const int64_t n_chunks = (E - R.S + R.CH - 1) / R.CH;
+  const int64_t n_ranges = R.Gs + n_chunks;
+  const int64_t Gp = n_chunks > 0 ? Gc : R.Gs;  // CTAs taking part
   const int c = blockIdx.x;
 
   // Segments without entries (context <= 0) are never streamed: zero them.
@@ -837,8 +968,7 @@ __global__ void __launch_bounds__(288, 1)
       for (int i = threadIdx.x; i < heads_cta * kD; i += HG * 32) orow[i] = from_f32<T>(0.f);
     }
   }
-  if (c >= Geff) return;  // uniform per CTA
-  const int64_t lo = flat_lo(c, E, Geff), hi = flat_lo(c + 1, E, Geff);
+  if (c >= Gp) return;  // uniform per CTA
 
   if (warp == HG) {
     // ------------------------------------------------------------ producer
@@ -870,6 +1000,16 @@ __global__ void __launch_bounds__(288, 1)
       ++it;
       return true;
     };
+    int* pool = tickets + (kTicketBytes / 4 - kPoolInts);
+    // first range: this CTA's static one, else a claimed chunk
+    int rng = c;
+    if (c >= R.Gs) {
+      int nr = INT_MAX;
+      if (lane == 0) nr = (int)R.Gs + atomicAdd(&pool[0], 1);
+      rng = __shfl_sync(0xffffffffu, nr, 0);
+    }
+    while (ok && rng < n_ranges) {
+    const int64_t lo = R.lo(rng), hi = R.lo(rng + 1);
     // segment containing lo: the largest s with cum[s] <= lo
     int s = 0;
     {
@@ -890,9 +1030,9 @@ __global__ void __launch_bounds__(288, 1)
       const int64_t segs = s_cum[s], sege = s_cum[s + 1];
       const int j0 = (int)(e - segs);
       const int j1 = (int)((hi < sege ? hi : sege) - segs);
-      const int c1 = flat_owner(segs, E, Geff), c2 = flat_owner(sege - 1, E, Geff);
+      const int c1 = R.of(segs), c2 = R.of(sege - 1);
       const int my_slot = first ? 0 : 1;
-      const int c1_slot = (segs == flat_lo(c1, E, Geff)) ? 0 : 1;
+      const int c1_slot = (segs == R.lo(c1)) ? 0 : 1;
       const int64_t ctx = s_ctx[b];
       const IDX* bt = block_table + b * p.max_blocks;
       // invalid entries before j0 shift the token ranks of this range
@@ -937,7 +1077,7 @@ __global__ void __launch_bounds__(288, 1)
         __syncwarp();
       }
       if (lane == 0 && ok) {
-        PageMeta m{1, 0, s, c1 == c2 ? -1 : my_slot, c1, c2, c1_slot, 0};
+        PageMeta m{1, 0, s, c1 == c2 ? -1 : my_slot, c1, c2, c1_slot, rng};
         ok = push(m, 0, 0);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -945,7 +1085,20 @@ __global__ void __launch_bounds__(288, 1)
       if (e == sege) ++s;
       first = false;
     }
+    // next range: a claimed chunk
+    int nr = INT_MAX;
+    if (lane == 0 && n_chunks > 0) nr = (int)R.Gs + atomicAdd(&pool[0], 1);
+    rng = __shfl_sync(0xffffffffu, nr, 0);
+    }
     if (lane == 0) {
+      if (n_chunks > 0) {
+        // every CTA of the grid ends here once; the last one re-arms the pool
+        const int done = atomicAdd(&pool[1], 1);
+        if (done == (int)Gp - 1) {
+          atomicExch(&pool[0], 0);
+          atomicExch(&pool[1], 0);
+        }
+      }
       if (ok) {
         PageMeta m{2, 0, 0, 0, 0, 0, 0, 0};
         ok = push(m, 0, 0);
@@ -964,14 +1117,13 @@ __global__ void __launch_bounds__(288, 1)
 
   // -------------------------------------------------------------- consumers
   const int w = warp;
-  const int qh = lane >> 2, qc = (lane & 3) * 2;
   const uint32_t base = sm100::smem_u32(smem);
   const uint32_t hbytes = p.stage_bytes / 4;
-  uint32_t qa[8][2];
-  float o[16][4];
-  float m_used = -INFINITY, l_part = 0.f;
+  uint32_t qb[8][2];
+  float o[8][4];
+  float mu[2] = {-INFINITY, -INFINITY}, lp[2] = {0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   int cur_seg = -1;
   const int nthr = HG * 32;
   for (int it = 0;; ++it) {
@@ -986,40 +1138,20 @@ __global__ void __launch_bounds__(288, 1)
       if (m.seg != cur_seg) {
         cur_seg = m.seg;
         const int64_t b = m.seg % B, kvh = (int64_t)(m.seg / B) * HG + w;
-        const T* qr = q + (b * p.Hq + kvh * G + (qh < G ? qh : 0)) * kD;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          qa[ks][0] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + qc) : 0u;
-          qa[ks][1] = qh < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + qc) : 0u;
-        }
+        load_q_frags<T, G>(q + (b * p.Hq + kvh * G) * kD, lane, qb);
       }
       const uint32_t kb = base + st * p.stage_bytes;
-      mma_page<T>(kb, kb + 2 * hbytes, m.ntok, w, bs, lane, hbytes, p.qscale, qa, o, m_used, l_part);
+      mma_page<T>(kb, kb + 2 * hbytes, m.ntok, w, bs, lane, hbytes, p.qscale, qb, o, mu, lp);
     } else if (m.kind == 1) {
       // ---- finish segment m.seg
-      float l = l_part;
-      l += __shfl_xor_sync(0xffffffffu, l, 1);
-      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      const float lA = head_sum(lp[0]), lB = head_sum(lp[1]);
       const int64_t b = m.seg % B, hg = m.seg / B;
-      const int64_t head = hg * heads_cta + w * G + qh;  // head index inside the sequence
+      const int64_t head0 = hg * heads_cta + w * G;  // first head of this warp inside the sequence
       if (m.slot < 0) {
-        if (qh < G) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          T* orow = out + (b * p.Hq + head) * kD;
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            *reinterpret_cast<uint32_t*>(orow + 8 * j + qc) = pack_pair<T>(o[j][0] * inv, o[j][1] * inv);
-        }
+        store_rows<T, G>(out + (b * p.Hq + head0) * kD, o, lA, lB, lane);
       } else {
-        if (qh < G) {
-          float* row = ws_rows + ((int64_t)(c * 2 + m.slot) * heads_cta + w * G + qh) * (kD + 2);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) *reinterpret_cast<float2*>(row + 8 * j + qc) = make_float2(o[j][0], o[j][1]);
-          if ((lane & 3) == 0) {
-            row[kD] = m_used;
-            row[kD + 1] = l;
-          }
-        }
+        float* row0 = ws_rows + ((int64_t)(m.rng * 2 + m.slot) * heads_cta + w * G) * kFlatPitch;
+        store_partial<G>(row0, kFlatPitch, row0 + kD, kFlatPitch, o, mu, lA, lB, lane);
         __threadfence();
         named_bar_sync(1, nthr);
         if (threadIdx.x == 0) {
@@ -1030,43 +1162,80 @@ __global__ void __launch_bounds__(288, 1)
         }
         named_bar_sync(1, nthr);
         if (s_flags[1]) {
+          // ---- merge the segment's pieces (ranges c1..c2): per-head max and
+          // 1/sum, then per-piece weights in shared memory and independent
+          // 16-byte loads of the pieces' o rows
           __threadfence();
-          for (int hh = threadIdx.x; hh < heads_cta; hh += nthr) {
-            float M = -INFINITY;
-            for (int cc = m.c1; cc <= m.c2; ++cc) {
-              const int sl = (cc == m.c1) ? m.c1_slot : 0;
-              M = fmaxf(M, __ldcg(ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * (kD + 2) + kD));
-            }
+          const int np = m.c2 - m.c1 + 1;
+          auto piece = [&](int i, int hh) -> const float* {
+            const int cc = m.c1 + i;
+            const int sl = (cc == m.c1) ? m.c1_slot : 0;
+            return ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * kFlatPitch;
+          };
+          for (int hh = w; hh < heads_cta; hh += HG) {
+            float mx = -INFINITY;
+            for (int i = lane; i < np; i += 32) mx = fmaxf(mx, __ldcg(piece(i, hh) + kD));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
             float L = 0.f;
-            for (int cc = m.c1; cc <= m.c2; ++cc) {
-              const int sl = (cc == m.c1) ? m.c1_slot : 0;
-              const float* r = ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * (kD + 2);
+            for (int i = lane; i < np; i += 32) {
+              const float* r = piece(i, hh);
               const float mc = __ldcg(r + kD);
-              L += (mc == -INFINITY) ? 0.f : exp2f(mc - M) * __ldcg(r + kD + 1);
+              L += (mc == -INFINITY) ? 0.f : exp2f(mc - mx) * __ldcg(r + kD + 1);
             }
-            s_comb[hh] = M;
-            s_comb[64 + hh] = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+            if (lane == 0) {
+              s_comb[hh] = mx;
+              s_comb[64 + hh] = L > 0.f ? 1.f / L : 0.f;
+            }
           }
           named_bar_sync(1, nthr);
-          for (int idx = threadIdx.x; idx < heads_cta * kD; idx += nthr) {
-            const int hh = idx / kD, d = idx % kD;
-            const float M = s_comb[hh], invL = s_comb[64 + hh];
-            float acc = 0.f;
-            for (int cc = m.c1; cc <= m.c2; ++cc) {
-              const int sl = (cc == m.c1) ? m.c1_slot : 0;
-              const float* r = ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * (kD + 2);
-              const float mc = __ldcg(r + kD);
-              if (mc != -INFINITY) acc = fmaf(exp2f(mc - M), __ldcg(r + d), acc);
+          float4 acc[G];
+#pragma unroll
+          for (int k = 0; k < G; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int i0 = 0; i0 < np; i0 += 32) {
+            const int nb = np - i0 < 32 ? np - i0 : 32;
+            for (int x = threadIdx.x; x < heads_cta * nb; x += nthr) {
+              const int hh = x / nb, i = x - hh * nb;
+              const float mc = __ldcg(piece(i0 + i, hh) + kD);
+              s_w[hh * 32 + i] = (mc == -INFINITY) ? 0.f : exp2f(mc - s_comb[hh]) * s_comb[64 + hh];
             }
-            out[(b * p.Hq + hg * heads_cta + hh) * kD + d] = from_f32<T>(acc * invL);
+            named_bar_sync(1, nthr);
+            for (int i = 0; i < nb; ++i) {
+              float4 v[G];
+#pragma unroll
+              for (int k = 0; k < G; ++k) {
+                const int idx = threadIdx.x + k * nthr;  // head idx / 32, dims 4 * (idx % 32)
+                v[k] = __ldcg(reinterpret_cast<const float4*>(piece(i0 + i, idx >> 5) + 4 * (idx & 31)));
+              }
+#pragma unroll
+              for (int k = 0; k < G; ++k) {
+                const int idx = threadIdx.x + k * nthr;
+                const float wgt = s_w[(idx >> 5) * 32 + i];
+                acc[k].x = fmaf(wgt, v[k].x, acc[k].x);
+                acc[k].y = fmaf(wgt, v[k].y, acc[k].y);
+                acc[k].z = fmaf(wgt, v[k].z, acc[k].z);
+                acc[k].w = fmaf(wgt, v[k].w, acc[k].w);
+              }
+            }
+            named_bar_sync(1, nthr);
           }
-          named_bar_sync(1, nthr);
+#pragma unroll
+          for (int k = 0; k < G; ++k) {
+            const int idx = threadIdx.x + k * nthr;
+            T* dst = out + (b * p.Hq + hg * heads_cta + (idx >> 5)) * kD + 4 * (idx & 31);
+            uint2 pk;
+            pk.x = pack_pair<T>(acc[k].x, acc[k].y);
+            pk.y = pack_pair<T>(acc[k].z, acc[k].w);
+            *reinterpret_cast<uint2*>(dst) = pk;
+          }
         }
       }
-      m_used = -INFINITY;
-      l_part = 0.f;
+      mu[0] = mu[1] = -INFINITY;
+      lp[0] = lp[1] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
       cur_seg = -1;
     }
     __syncwarp();
@@ -1080,6 +1249,8 @@ struct Geometry {
   bool mma;   // tensor-core consumer (block size a multiple of 16)
   bool flat;  // persistent flat-partition kernel
   int flat_grid;
+  int dyn_pct, chunk;  // persistent kernel: claimed share of the entries, entries per chunk
+  int64_t max_blocks_all;
   size_t flat_smem;
   int HG, n_hg, G, split_blocks, max_splits, stages;
   uint32_t stage_bytes;
@@ -1099,6 +1270,7 @@ Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t 
   if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
   g.split_blocks = split;
   g.max_splits = (int)((max_blocks + split - 1) / split);
+  g.max_blocks_all = max_blocks;
   if (D != kD || !(g.G == 1 || g.G == 2 || g.G == 4 || g.G == 8) || bs > 256 || bs < 1 ||
       g.max_splits > kMaxSplits)
     return g;
@@ -1136,8 +1308,12 @@ Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t 
   g.flat = g.mma && nseg <= kFlatMaxSeg && !(cfg && (cfg->flags & 2));
   if (g.flat) {
     g.flat_grid = (cfg && cfg->tile_m > 0) ? cfg->tile_m : device_sm_count();
+    // flags bit 2: equal static ranges only; tile_k: claimed percent; tile_n: entries per chunk
+    g.dyn_pct = (cfg && (cfg->flags & 4)) ? 0 : (cfg && cfg->tile_k > 0 ? (cfg->tile_k < 90 ? cfg->tile_k : 90)
+                                                                           : kFlatDynPct);
+    g.chunk = (cfg && cfg->tile_n > 0) ? cfg->tile_n : kFlatChunk;
     const size_t extra = (size_t)g.stages * (2 * 8 + sizeof(PageMeta)) + (size_t)(nseg + 1) * 8 +
-                         (size_t)B * 8 + 64 * 4 + 128 * 4 + 16;
+                         (size_t)B * 8 + 64 * 4 + 128 * 4 + 16 + (size_t)g.HG * g.G * 32 * 4;
     g.flat_smem = (size_t)g.stages * g.stage_bytes + extra + 1024;
     if (g.flat_smem > kSmemBudget) g.flat = false;
   }
@@ -1206,6 +1382,9 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
     fp.n_hg = geo.n_hg;
     fp.stages = geo.stages;
     fp.nseg = (int)(geo.n_hg * B);
+    fp.dyn_pct = geo.dyn_pct;
+    fp.chunk = geo.chunk;
+    fp.max_chunks = kFlatChunksPerCta * geo.flat_grid;
     fp.stage_bytes = geo.stage_bytes;
     fp.qscale = scale * 1.4426950408889634f;
     auto fk = paged_decode_flat_kernel<T, IDX, G>;
@@ -1230,7 +1409,10 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
 
 size_t workspace_bytes_for(int64_t B, int64_t Hq, int64_t D, const Geometry& geo) {
   if (!geo.tma_path) return 0;
-  if (geo.flat) return kTicketBytes + (size_t)geo.flat_grid * 2 * geo.HG * geo.G * (size_t)(D + 2) * 4;
+  if (geo.flat)
+    return kTicketBytes + (size_t)flat_partial_rows(geo.flat_grid, (int64_t)geo.n_hg * B * geo.max_blocks_all,
+                                                    geo.dyn_pct, geo.chunk, (int64_t)geo.HG * geo.G) *
+                              (size_t)kFlatPitch * 4;
   const size_t n_rows = (size_t)B * Hq * geo.max_splits;
   return kTicketBytes + n_rows * (size_t)(D + 2) * 4;
 }
@@ -1252,10 +1434,19 @@ extern "C" size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq, int
   g.tma_path = true;
   g.max_splits = (int)((max_blocks + split - 1) / split);
   const size_t split_need = workspace_bytes_for(B, Hq, D, g);
-  // persistent kernel: two partial slots per CTA of at most min(Hq, 64) heads
+  // persistent kernel: two partial slots per range (one static range per CTA
+  // plus the claimed chunks) of at most min(Hq, 64) heads; the chunks of all
+  // head groups together hold at most B * max_blocks * Hq * pct / 100 head-pages
   const int64_t grid = (cfg && cfg->tile_m > 0) ? cfg->tile_m : device_sm_count();
   const int64_t heads = Hq < 64 ? Hq : 64;
-  const size_t flat_need = kTicketBytes + (size_t)grid * 2 * heads * (size_t)(D + 2) * 4;
+  const int pct = (cfg && (cfg->flags & 4)) ? 0 : (cfg && cfg->tile_k > 0 ? (cfg->tile_k < 90 ? cfg->tile_k : 90)
+                                                                            : kFlatDynPct);
+  const int64_t ch = (cfg && cfg->tile_n > 0) ? cfg->tile_n : kFlatChunk;
+  const int64_t dyn_heads = B * max_blocks * Hq * pct / 100 + heads;
+  int64_t rows = 2 * ((grid + 4) * heads + dyn_heads / ch + 1);
+  const int64_t rows_cap = 2 * (grid + kFlatChunksPerCta * grid + 4) * heads;
+  if (pct > 0 && rows > rows_cap) rows = rows_cap;
+  const size_t flat_need = kTicketBytes + (size_t)rows * (size_t)kFlatPitch * 4;
   return split_need > flat_need ? split_need : flat_need;
 }
 
@@ -1279,7 +1470,12 @@ extern "C" int b200_paged_attention(const void* q, const void* k_cache, const vo
   Geometry geo = choose_geometry(B, Hq, Hkv, D, block_size, max_blocks, cfg);
   const bool aligned = aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out);
   if (geo.tma_path && aligned && num_blocks * block_size < (1ll << 31)) {
-    const size_t need = workspace_bytes_for(B, Hq, D, geo);
+    size_t need = workspace_bytes_for(B, Hq, D, geo);
+    if (geo.flat && geo.dyn_pct > 0 && workspace_bytes < need) {
+      // too little scratch for the claimed chunks' partials: equal static ranges
+      geo.dyn_pct = 0;
+      need = workspace_bytes_for(B, Hq, D, geo);
+    }
     const bool single = geo.max_splits == 1 && !geo.flat;
     if (!single && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
       return B200_ERR_WORKSPACE;
