@@ -207,6 +207,22 @@ __device__ __forceinline__ float round_bits_to(float v) {
   }
 }
 
+// Rounds two floats to T's precision (round half to even) in place: one
+// packed conversion and two widenings for the 16-bit types, nothing for fp32.
+template <typename T>
+__device__ __forceinline__ void round_pair_to(float& a, float& b) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+    a = __uint_as_float(u << 16);
+    b = __uint_as_float(u & 0xFFFF0000u);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    const float2 f = __half22float2(__floats2half2_rn(a, b));
+    a = f.x;
+    b = f.y;
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ int quant_code_fast(float x, float s, float r) {
   const float q0 = __fmul_rn(x, r);

@@ -7,7 +7,10 @@
 // held in registers between the sum-of-squares pass and the scaling pass, so
 // x is never re-read.  Loads and stores are 16-byte vectors with the
 // streaming cache hint (x and y are touched exactly once; w stays in L1/L2).
+#include <type_traits>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace b200 {
 namespace {
@@ -51,7 +54,9 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_kernel(const T* __restrict__
   const int nvec = D / VN;
 
   uint4 raw[NV];
-  float ss = 0.f;
+  // sum of squares in two fp32 lanes (even / odd elements, one fp32x2 FMA
+  // per pair), the same order as rmsnorm_quant_row_kernel's
+  float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
@@ -60,10 +65,10 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_kernel(const T* __restrict__
       float f[VN];
       unpack16<T>(raw[i], f);
 #pragma unroll
-      for (int j = 0; j < VN; ++j) ss = fmaf(f[j], f[j], ss);
+      for (int j = 0; j < VN; j += 2) sm100::ffma2(ss0, ss1, f[j], f[j + 1], f[j], f[j + 1], ss0, ss1);
     }
   }
-  ss = block_sum(ss, red);
+  const float ss = block_sum(ss0 + ss1, red);
   // mean then 1/sqrt, both IEEE-rounded, as torch.rsqrt(x.pow(2).mean() + eps).
   const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
 
@@ -75,7 +80,10 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_kernel(const T* __restrict__
       unpack16<T>(raw[i], f);
       load_weights<W, VN>(w + (int64_t)v * VN, wf);
 #pragma unroll
-      for (int j = 0; j < VN; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], rstd), wf[j]);
+      for (int j = 0; j < VN; j += 2) {
+        sm100::fmul2_bcast(o[j], o[j + 1], f[j], f[j + 1], rstd);
+        sm100::fmul2(o[j], o[j + 1], o[j], o[j + 1], wf[j], wf[j + 1]);
+      }
       stg_stream16(yr + (int64_t)v * VN, pack16<T>(o));
     }
   }
@@ -100,70 +108,143 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // the quantiser's dtype rounding (bit-identical to quantising the rmsnorm
 // output).  One pass over x: x is read once, q (1 B per element) and the
 // scale are written, y only when asked for.
-template <typename T, typename W, int NV>
-__global__ void __launch_bounds__(1024) rmsnorm_quant_row_kernel(const T* __restrict__ x, const W* __restrict__ w,
+// Block reductions of R rows at once (one barrier for all of them), each row
+// in block_sum's / block_max's order.
+template <int R>
+__device__ __forceinline__ void block_sum_rows(float (&v)[R], float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = warp_sum(v[r]);
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) red[r * 32 + warp] = v[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = warp_sum((lane < nwarps) ? red[r * 32 + lane] : 0.f);
+}
+
+template <int R>
+__device__ __forceinline__ void block_max_rows(float (&v)[R], float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = warp_max(v[r]);
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) red[r * 32 + warp] = v[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = warp_max((lane < nwarps) ? red[r * 32 + lane] : 0.f);
+}
+
+template <typename T, typename W, int NV, int R>
+__global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(const T* __restrict__ x, const W* __restrict__ w,
                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                 T* __restrict__ y, int D, float eps) {
+                                                                 T* __restrict__ y, int64_t rows, int D, float eps) {
   constexpr int VN = Vec<T>::N;
-  __shared__ float red[32];
-  __shared__ float red2[32];
-  const int64_t row = blockIdx.x;
-  const T* xr = x + row * D;
+  __shared__ float red[R * 32];
+  __shared__ float red2[R * 32];
+  const int64_t row0 = (int64_t)blockIdx.x * R;
   const int nvec = D / VN;
-  uint4 raw[NV];
-  float ss = 0.f;
+  // The rows stay in registers: as fp32 when they fit in 32 floats per
+  // thread (x, then y rounded to T), else packed as T and widened per pass.
+  constexpr bool kF32 = NV * VN * R <= 32;
+  float f[kF32 ? R : 1][kF32 ? NV : 1][VN];
+  uint4 raw[kF32 ? 1 : R][kF32 ? 1 : NV];
+  auto row_f = [&](int r, int i) -> float* { return f[kF32 ? r : 0][kF32 ? i : 0]; };
+  auto live = [&](int r, int v) { return v < nvec && row0 + r < rows; };
+  float ss[R];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = threadIdx.x + i * blockDim.x;
-    if (v < nvec) {
-      raw[i] = ldg_stream16(xr + (int64_t)v * VN);
-      float f[VN];
-      unpack16<T>(raw[i], f);
+  for (int r = 0; r < R; ++r) {
+    float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
-      for (int j = 0; j < VN; ++j) ss = fmaf(f[j], f[j], ss);
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * blockDim.x;
+      if (live(r, v)) {
+        const uint4 u = ldg_stream16(x + (row0 + r) * D + (int64_t)v * VN);
+        if constexpr (!kF32) raw[r][i] = u;
+        float* fi = row_f(r, i);
+        unpack16<T>(u, fi);
+#pragma unroll
+        for (int j = 0; j < VN; j += 2) sm100::ffma2(ss0, ss1, fi[j], fi[j + 1], fi[j], fi[j + 1], ss0, ss1);
+      }
+    }
+    ss[r] = ss0 + ss1;
+  }
+  block_sum_rows<R>(ss, red);
+  float amax[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss[r], (float)D), eps));
+    amax[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * blockDim.x;
+      if (live(r, v)) {
+        float* fi = row_f(r, i);
+        if constexpr (!kF32) unpack16<T>(raw[r][i], fi);
+        float wf[VN];
+        load_weights<W, VN>(w + (int64_t)v * VN, wf);
+#pragma unroll
+        for (int j = 0; j < VN; j += 2) {
+          sm100::fmul2_bcast(fi[j], fi[j + 1], fi[j], fi[j + 1], rstd);
+          sm100::fmul2(fi[j], fi[j + 1], fi[j], fi[j + 1], wf[j], wf[j + 1]);
+        }
+        const uint4 u = pack16<T>(fi);  // y rounded to T, kept for the quantiser
+        if constexpr (!kF32) raw[r][i] = u;
+        unpack16<T>(u, fi);
+#pragma unroll
+        for (int j = 0; j < VN; j += 2) amax[r] = sm100::fmax3(amax[r], fabsf(fi[j]), fabsf(fi[j + 1]));
+        if (y != nullptr) stg_stream16(y + (row0 + r) * D + (int64_t)v * VN, u);
+      }
     }
   }
-  ss = block_sum(ss, red);
-  const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
-  float amax = 0.f;
+  block_max_rows<R>(amax, red2);
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = threadIdx.x + i * blockDim.x;
-    if (v < nvec) {
-      float f[VN], wf[VN];
-      unpack16<T>(raw[i], f);
-      load_weights<W, VN>(w + (int64_t)v * VN, wf);
+  for (int r = 0; r < R; ++r) {
+    if (row0 + r >= rows) break;
+    const float s = finish_scale<T>(amax[r]);
+    const float rs = __frcp_rn(s);
+    if (threadIdx.x == 0) scale[row0 + r] = s;
+    int8_t* qr = q + (row0 + r) * D;
 #pragma unroll
-      for (int j = 0; j < VN; ++j) f[j] = __fmul_rn(__fmul_rn(f[j], rstd), wf[j]);
-      raw[i] = pack16<T>(f);  // y rounded to T, kept for the quantiser
-      unpack16<T>(raw[i], f);
+    for (int i = 0; i < NV; ++i) {
+      const int v = threadIdx.x + i * blockDim.x;
+      if (v < nvec) {
+        float* fi = row_f(r, i);
+        if constexpr (!kF32) unpack16<T>(raw[r][i], fi);
+        // quant_code_fast on pairs: q0 = RN(y r), e = y - q0 s, RN(q0 + e r) =
+        // RN(y / s); clamp to [-127, 127] first (the bounds are representable
+        // in T, and rounding is monotone, so clamp-then-round equals the
+        // reference's round-then-clamp), round the pair to T's precision with
+        // one packed conversion and widen it back, add 1.5 * 2^23 so the low
+        // byte of the bits is the two's-complement code of rint
+        uint32_t m[VN];
 #pragma unroll
-      for (int j = 0; j < VN; ++j) amax = fmaxf(amax, fabsf(f[j]));
-      if (y != nullptr) stg_stream16(y + row * D + (int64_t)v * VN, raw[i]);
-    }
-  }
-  const float s = finish_scale<T>(block_max(amax, red2));
-  const float rs = __frcp_rn(s);
-  if (threadIdx.x == 0) scale[row] = s;
-  int8_t* qr = q + row * D;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = threadIdx.x + i * blockDim.x;
-    if (v < nvec) {
-      float f[VN];
-      unpack16<T>(raw[i], f);
-      int8_t c[VN];
-#pragma unroll
-      for (int j = 0; j < VN; ++j) c[j] = (int8_t)quant_code_fast<T>(f[j], s, rs);
-      // VN codes: 8 bytes for 16-bit T, 4 for fp32
-      if constexpr (VN == 8) {
-        uint2 pk;
-        memcpy(&pk, c, 8);
-        *reinterpret_cast<uint2*>(qr + (int64_t)v * VN) = pk;
-      } else {
-        uint32_t pk;
-        memcpy(&pk, c, 4);
-        *reinterpret_cast<uint32_t*>(qr + (int64_t)v * VN) = pk;
+        for (int j = 0; j < VN; j += 2) {
+          float q0, q1, e0, e1, v0, v1;
+          sm100::fmul2_bcast(q0, q1, fi[j], fi[j + 1], rs);
+          sm100::ffma2(e0, e1, q0, q1, -s, -s, fi[j], fi[j + 1]);
+          sm100::ffma2(v0, v1, e0, e1, rs, rs, q0, q1);
+          v0 = fmaxf(fminf(v0, 127.f), -127.f);
+          v1 = fmaxf(fminf(v1, 127.f), -127.f);
+          round_pair_to<T>(v0, v1);
+          sm100::ffma2_bcast(v0, v1, v0, v1, 1.0f, 12582912.0f);
+          m[j] = __float_as_uint(v0);
+          m[j + 1] = __float_as_uint(v1);
+        }
+        if constexpr (VN == 8) {
+          uint2 pk;
+          pk.x = __byte_perm(__byte_perm(m[0], m[1], 0x0040), __byte_perm(m[2], m[3], 0x0040), 0x5410);
+          pk.y = __byte_perm(__byte_perm(m[4], m[5], 0x0040), __byte_perm(m[6], m[7], 0x0040), 0x5410);
+          *reinterpret_cast<uint2*>(qr + (int64_t)v * VN) = pk;
+        } else {
+          const uint32_t pk = __byte_perm(__byte_perm(m[0], m[1], 0x0040), __byte_perm(m[2], m[3], 0x0040), 0x5410);
+          *reinterpret_cast<uint32_t*>(qr + (int64_t)v * VN) = pk;
+        }
       }
     }
   }
@@ -257,6 +338,12 @@ extern "C" int b200_rmsnorm(const void* x, const void* weight, void* y, int64_t 
   return B200_ERR_UNSUPPORTED;
 }
 
+namespace b200 {
+namespace {
+constexpr int kQuantRowsPerCta = 1;  // measured: 2 and 4 rows per CTA run 9% and 50% slower at 16384 x 4096
+}  // namespace
+}  // namespace b200
+
 extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t* q, float* scale, void* y,
                                        int64_t rows, int64_t D, float eps, int32_t dtype, int32_t weight_dtype,
                                        const b200_launch_cfg* cfg, void* stream) {
@@ -288,12 +375,30 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     const T* xp = static_cast<const T*>(x);
     const W* wp = static_cast<const W*>(weight);
     T* yp = static_cast<T*>(y);
-    dim3 grid((unsigned)rows);
-    if (nv <= 1) rmsnorm_quant_row_kernel<T, W, 1><<<grid, threads, 0, s>>>(xp, wp, q, scale, yp, (int)D, eps);
-    else if (nv <= 2) rmsnorm_quant_row_kernel<T, W, 2><<<grid, threads, 0, s>>>(xp, wp, q, scale, yp, (int)D, eps);
-    else if (nv <= 4) rmsnorm_quant_row_kernel<T, W, 4><<<grid, threads, 0, s>>>(xp, wp, q, scale, yp, (int)D, eps);
-    else rmsnorm_quant_row_kernel<T, W, 8><<<grid, threads, 0, s>>>(xp, wp, q, scale, yp, (int)D, eps);
-    return launch_status(cudaGetLastError());
+    // rows per CTA (rows_per_cta: 1, 2 or 4): more bytes in flight per CTA
+    // and one barrier pair for all of them
+    int R = (cfg && cfg->rows_per_cta > 0) ? cfg->rows_per_cta : kQuantRowsPerCta;
+    if (R != 1 && R != 2 && R != 4) return B200_ERR_BAD_ARG;
+    if (nv > 4 || threads > 256) R = 1;  // multi-row CTAs are compiled for <= 256 threads
+    auto go = [&](auto nv_tag, auto r_tag) -> int {
+      constexpr int NV = decltype(nv_tag)::value, RR = decltype(r_tag)::value;
+      const dim3 grid((unsigned)((rows + RR - 1) / RR));
+      rmsnorm_quant_row_kernel<T, W, NV, RR><<<grid, threads, 0, s>>>(xp, wp, q, scale, yp, rows, (int)D, eps);
+      return launch_status(cudaGetLastError());
+    };
+    using I1 = std::integral_constant<int, 1>;
+    using I2 = std::integral_constant<int, 2>;
+    using I4 = std::integral_constant<int, 4>;
+    using I8 = std::integral_constant<int, 8>;
+    auto by_r = [&](auto nv_tag) -> int {
+      if (R == 1) return go(nv_tag, I1{});
+      if (R == 2) return go(nv_tag, I2{});
+      return go(nv_tag, I4{});
+    };
+    if (nv <= 1) return by_r(I1{});
+    if (nv <= 2) return by_r(I2{});
+    if (nv <= 4) return by_r(I4{});
+    return go(I8{}, I1{});
   };
   if (weight_dtype == dtype)
     return B200_DISPATCH_FLOAT(dtype, [&] { return run(scalar_t{}, scalar_t{}); });

@@ -425,6 +425,17 @@ __device__ __forceinline__ void fadd2_acc(float& s0, float& s1, float a0, float 
       : "f"(a0), "f"(a1));
 }
 
+// (a0, a1) * (b0, b1) as one fp32x2 instruction.
+__device__ __forceinline__ void fmul2(float& y0, float& y1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(y0), "=f"(y1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // (a0, a1) * (b, b) as one fp32x2 instruction.
 __device__ __forceinline__ void fmul2_bcast(float& y0, float& y1, float a0, float a1, float b) {
   asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
