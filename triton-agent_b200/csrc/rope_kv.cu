@@ -26,6 +26,7 @@
 // after its own and skips its write if a later pair targets the same row, so
 // the result does not depend on CTA scheduling.
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace b200 {
 namespace {
@@ -290,6 +291,9 @@ __global__ void __launch_bounds__(1024) rope_kv_append_paged_fast_kernel(
     float x1[VN], x2[VN], y1[VN], y2[VN];
     unpack16<T>(a, x1);
     unpack16<T>(b, x2);
+    // every product rounded on its own, as eager fp32 does (scalar .rn
+    // operations: the assembler contracts an fp32x2 multiply feeding an
+    // fp32x2 add into one fused multiply-add)
 #pragma unroll
     for (int j = 0; j < VN; ++j) {
       y1[j] = __fsub_rn(__fmul_rn(x1[j], cv[j]), __fmul_rn(x2[j], sv[j]));

@@ -389,6 +389,12 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// fp32x2 helpers.  Each instruction rounds like its scalar .rn form
+// (checked on 4M random pairs), but the assembler contracts an fp32x2
+// multiply whose result feeds an fp32x2 add or subtract into one fused
+// multiply-add (one rounding), .rn or not; where eager two-rounding results
+// are required, multiply-then-add must stay scalar (__fmul_rn / __fadd_rn).
+
 // (a0, a1) * (b, b) + (c, c) as one fp32x2 instruction.
 __device__ __forceinline__ void ffma2_bcast(float& y0, float& y1, float a0, float a1, float b, float c) {
   asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
