@@ -747,6 +747,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!sm100::mbar_wait_warp(sm100::smem_u32(bars.mma_done), 0) && leader) b200_dev_error(kDevErrTimeoutMma);
   } else {
     const int quarter = warp & 3;
+    // the dequant scales are loaded before the accumulators are ready (after
+    // an L2 flush each is a DRAM round trip that would otherwise sit on the
+    // kernel's tail): sA once, sW per segment before its accumulator wait
+    constexpr int kSa = MN <= 32 ? MN : 1;
+    float sa[kSa];
+#pragma unroll
+    for (int m = 0; m < kSa; ++m) sa[m] = (MN <= 32 && m < p.M) ? __ldg(&sA[m]) : 0.f;
     int seg = 0;
     for (int64_t u = u0; u < u1; ++seg) {
       const int n_tile = (int)(u / p.k_groups);
@@ -754,6 +761,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int count = (int)(seg_end - u);
       u = seg_end;
       const int b = seg & 1;
+      const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
+      const float sw = (count == p.k_groups && n < p.N) ? __ldg(&sW[n]) : 0.f;
       const bool ok = sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_full[b]), (seg >> 1) & 1);
       if (!ok) {
         set_abort(bars, kDevErrTimeoutMma);
@@ -763,31 +772,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc[MN];
 #pragma unroll
       for (int j = 0; j < MN; ++j) acc[j] = 0;
+      const uint32_t t_row = tmem + b * kCols + ((uint32_t)(quarter * 32) << 16);
+      if constexpr (MN == 16) {
+        // all chains' loads in flight, one wait
+        uint32_t part[kChains][16];
 #pragma unroll
-      for (int ch = 0; ch < kChains; ++ch) {
-        uint32_t part[MN];
+        for (int ch = 0; ch < kChains; ++ch) sm100::tmem_ld_32x32b_x16(t_row + ch * kChainCols, part[ch]);
 #pragma unroll
-        for (int c = 0; c < MN; c += 16)
-          sm100::tmem_ld_32x32b_x16(tmem + b * kCols + ch * kChainCols + ((uint32_t)(quarter * 32) << 16) + c,
-                                    part + c);
+        for (int ch = 0; ch < kChains; ++ch) sm100::tmem_wait_ld_regs16(part[ch]);
 #pragma unroll
-        for (int c = 0; c < MN; c += 16) sm100::tmem_wait_ld_regs16(part + c);
+        for (int ch = 0; ch < kChains; ++ch)
 #pragma unroll
-        for (int j = 0; j < MN; ++j) acc[j] += part[j];
+          for (int j = 0; j < 16; ++j) acc[j] += part[ch][j];
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < kChains; ++ch) {
+          uint32_t part[MN];
+#pragma unroll
+          for (int c = 0; c < MN; c += 16) sm100::tmem_ld_32x32b_x16(t_row + ch * kChainCols + c, part + c);
+#pragma unroll
+          for (int c = 0; c < MN; c += 16) sm100::tmem_wait_ld_regs16(part + c);
+#pragma unroll
+          for (int j = 0; j < MN; ++j) acc[j] += part[j];
+        }
       }
       // the buffer is in registers: hand it back to the MMA warp
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&bars.acc_empty[b]));
-      const int64_t n = (int64_t)n_tile * BM + quarter * 32 + lane;  // output column (TMEM lane)
       const bool n_ok = n < p.N && !aborted(bars);
       if (count == p.k_groups) {
         if (n_ok) {
-          const float sw = sW[n];
 #pragma unroll
           for (int m = 0; m < MN; ++m) {
             if (m < p.M) {
-              C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant(acc[m], sA[m], sw));
+              const float am = MN <= 32 ? sa[m < kSa ? m : 0] : __ldg(&sA[m]);
+              C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant(acc[m], am, sw));
               if (acc_out) acc_out[(int64_t)m * p.N + n] = (int32_t)acc[m];
             }
           }
@@ -814,15 +834,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last) {
           __threadfence();
           if (n_ok) {
-            const float sw = sW[n];
+            const float sw_t = __ldg(&sW[n]);
+            int32_t v[MN];
+#pragma unroll
+            for (int m = 0; m < MN; ++m) v[m] = m < p.M ? __ldcg(&ws[(int64_t)m * p.N + n]) : 0;
 #pragma unroll
             for (int m = 0; m < MN; ++m) {
               if (m < p.M) {
-                int32_t* cell = &ws[(int64_t)m * p.N + n];
-                const int32_t v = __ldcg(cell);
-                *cell = 0;  // ready for the next call
-                C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant((uint32_t)v, sA[m], sw));
-                if (acc_out) acc_out[(int64_t)m * p.N + n] = v;
+                ws[(int64_t)m * p.N + n] = 0;  // ready for the next call
+                const float am = MN <= 32 ? sa[m < kSa ? m : 0] : __ldg(&sA[m]);
+                C[(int64_t)m * p.ldc + n] = from_f32<OutT>(dequant((uint32_t)v[m], am, sw_t));
+                if (acc_out) acc_out[(int64_t)m * p.N + n] = v[m];
               }
             }
           }
