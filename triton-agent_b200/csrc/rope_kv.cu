@@ -307,6 +307,98 @@ __global__ void __launch_bounds__(1024) rope_kv_append_paged_fast_kernel(
   }
 }
 
+// Prefill-size variant (ownership table given): a thread covers the same
+// 16-byte column chunk c of RPT rows of one token (rows g, g + G, ...), so
+// the token's cos/sin chunk is loaded once per thread instead of once per
+// row, and the per-thread setup (slot, position, addresses) is shared by RPT
+// rows.  Several tokens per CTA; every source load of the thread is issued
+// before the ownership check and the barrier.
+template <typename T, typename CS, int RPT>
+__global__ void __launch_bounds__(256) rope_kv_append_paged_rows_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const int64_t* __restrict__ positions, const CS* __restrict__ cos,
+    const CS* __restrict__ sin, int64_t cs_rows, const int64_t* __restrict__ slots,
+    T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t n_tok,
+    int Hq, int Hkv, int64_t D, int64_t slot_hi, int cpr, int groups, int* __restrict__ owner) {
+  constexpr int VN = Vec<T>::N;
+  __shared__ int s_hit[32];
+  const int tpt = cpr * groups;  // threads per token
+  const int lt = threadIdx.x / tpt;
+  const int rem = threadIdx.x - lt * tpt;
+  const int c = rem % cpr, g = rem / cpr;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x / tpt) + lt;
+  const bool live = t < n_tok && lt < 32;
+  const int64_t half = D / 2;
+  const int nq = q ? Hq : 0;
+  const int total_rows = nq + 2 * Hkv;
+  int64_t pos = 0, slot = -1;
+  uint4 a[RPT], b[RPT];
+  if (live) {
+    pos = positions ? __ldg(&positions[t]) : t;
+    slot = __ldg(&slots[t]);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int row = g + groups * i;
+      if (row < total_rows) {
+        const T* src = row < nq ? q + (t * Hq + row) * D
+                                : (row < nq + Hkv ? k + (t * Hkv + (row - nq)) * D
+                                                  : v + (t * Hkv + (row - nq - Hkv)) * D);
+        a[i] = __ldg(reinterpret_cast<const uint4*>(src + c * VN));
+        b[i] = __ldg(reinterpret_cast<const uint4*>(src + half + c * VN));
+      }
+    }
+    if (rem == 0) {
+      int hit = 0;
+      if (slot >= 0 && slot < slot_hi) {
+        const int o = *(volatile int*)&owner[slot];
+        hit = o != (int)(t + 1);
+        if (!hit) owner[slot] = 0;  // back to zero for the next call (later readers are not owners)
+      }
+      s_hit[lt] = hit;
+    }
+  }
+  const bool pos_ok = pos >= 0 && pos < cs_rows;
+  if (!pos_ok) pos = 0;
+  float cv[VN], sv[VN];
+  if (live && g < nq + Hkv) {  // the thread has at least one rotated row (row g)
+    load_cs<CS, VN>(cos + pos * D + c * VN, cv);
+    load_cs<CS, VN>(sin + pos * D + c * VN, sv);
+  }
+  __syncthreads();
+  if (!live) return;
+  const bool write_kv = pos_ok && slot >= 0 && slot < slot_hi && !s_hit[lt];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int row = g + groups * i;
+    if (row >= total_rows) continue;
+    T* dst;
+    if (row < nq) {
+      if (!pos_ok) continue;
+      dst = q_out + (t * Hq + row) * D;
+    } else {
+      if (!write_kv) continue;
+      dst = (row < nq + Hkv) ? k_cache + (slot * Hkv + (row - nq)) * D
+                             : v_cache + (slot * Hkv + (row - nq - Hkv)) * D;
+    }
+    if (row < nq + Hkv) {
+      float x1[VN], x2[VN], y1[VN], y2[VN];
+      unpack16<T>(a[i], x1);
+      unpack16<T>(b[i], x2);
+      // every product rounded on its own, as eager fp32 does
+#pragma unroll
+      for (int j = 0; j < VN; ++j) {
+        y1[j] = __fsub_rn(__fmul_rn(x1[j], cv[j]), __fmul_rn(x2[j], sv[j]));
+        y2[j] = __fadd_rn(__fmul_rn(x2[j], cv[j]), __fmul_rn(x1[j], sv[j]));
+      }
+      *reinterpret_cast<uint4*>(dst + c * VN) = pack16<T>(y1);
+      *reinterpret_cast<uint4*>(dst + half + c * VN) = pack16<T>(y2);
+    } else {
+      *reinterpret_cast<uint4*>(dst + c * VN) = a[i];
+      *reinterpret_cast<uint4*>(dst + half + c * VN) = b[i];
+    }
+  }
+}
+
 int threads_for(int64_t rows, int tpr, const b200_launch_cfg* cfg) {
   int64_t want = rows * tpr;
   int threads = (cfg && cfg->threads > 0) ? cfg->threads : (int)((want + 31) / 32 * 32);
@@ -504,6 +596,23 @@ int launch_fused(const void* q, const void* k, const void* v, const int64_t* pos
     if (owner != nullptr) {
       slot_owner_kernel<<<(unsigned)((n_tok + 255) / 256), 256, 0, s>>>(slots, n_tok, slot_hi, owner);
       if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return launch_status(e);
+    }
+    // prefill sizes (ownership table): RPT rows per thread, several tokens per
+    // CTA; rows kernel when the row count splits into <= 8 row groups of
+    // 16-byte chunks that fit a 256-thread CTA
+    if (owner != nullptr && half / VN <= 32) {
+      const int cpr = (int)(half / VN);
+      constexpr int kRpt = 6;
+      const int groups = (int)((rows + kRpt - 1) / kRpt);
+      const int tpt = cpr * groups;
+      if (tpt <= 256 && 256 / tpt <= 32) {  // at most 32 tokens per CTA (s_hit)
+        const int tpc = 256 / tpt;
+        const int64_t grid = (n_tok + tpc - 1) / tpc;
+        rope_kv_append_paged_rows_kernel<T, CS, kRpt><<<(unsigned)grid, tpc * tpt, 0, s>>>(
+            qp, kp, vp, positions, cp, sp, cs_rows, slots, qo, kc, vc, n_tok, (int)Hq, (int)Hkv, D, slot_hi, cpr,
+            groups, owner);
+        return launch_status(cudaGetLastError());
+      }
     }
     rope_kv_append_paged_fast_kernel<T, CS><<<(unsigned)n_tok, th, 0, s>>>(
         qp, kp, vp, positions, cp, sp, cs_rows, slots, qo, kc, vc, n_tok, (int)Hq, (int)Hkv, D, slot_hi, tpr,
