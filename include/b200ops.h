@@ -99,7 +99,10 @@ int b200_rmsnorm(const void* x, const void* weight, void* y, int64_t rows,
  * equal b200_rmsnorm's output up to the order of the fp32 sum of squares.
  * One pass over x.  q: [rows, D] int8 (8-byte aligned); scale: [rows]
  * f32; y (nullable): [rows, D] of `dtype`.  Needs D % (16 / sizeof(dtype))
- * == 0 and 16-byte aligned x/weight/y (B200_ERR_ALIGNMENT otherwise). */
+ * == 0 and 16-byte aligned x/weight/y (B200_ERR_ALIGNMENT otherwise).
+ * cfg: threads (CTA size, multiple of 32, default about D / 32 for 16-bit
+ * dtypes), rows_per_cta (1, 2 or 4 rows per CTA; more than one only with at
+ * most 256 threads; default 1). */
 int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t* q, float* scale,
                             void* y, int64_t rows, int64_t D, float eps, int32_t dtype,
                             int32_t weight_dtype, const b200_launch_cfg* cfg, void* stream);
@@ -171,7 +174,8 @@ int b200_rope_kv_append_paged(const void* q, const void* k, const void* v,
  * zero-filled before its first use and returned to zero by each call.  A
  * later token writing the same slot wins, as in the reference's loop, in
  * O(T) instead of a per-token scan of all later slots.  slot_owner NULL is
- * b200_rope_kv_append_paged. */
+ * b200_rope_kv_append_paged.  cfg (table path): rows_per_cta = rows of a
+ * token per thread (2, 3, 4, 6, 8 or 12; default 4). */
 int b200_rope_kv_append_paged_ws(const void* q, const void* k, const void* v,
                                  const int64_t* positions, const void* cos, const void* sin,
                                  int64_t cs_rows, const int64_t* slot_mapping, void* q_out,
@@ -191,7 +195,13 @@ int b200_rope_kv_append_paged_ws(const void* q, const void* k, const void* v,
  * Softmax and accumulation in fp32.  workspace: device buffer of at least
  * b200_paged_attention_workspace_size() bytes, zero-filled once before first
  * use (the kernel leaves it ready for the next call).
- * cfg: split (KV blocks per split, default 32), stages (default 3). */
+ * cfg: split (KV blocks per split of the split-grid kernel, default 64),
+ * stages (ring depth, default as many 3+ as fit), rows_per_cta (kv heads per
+ * CTA, <= 8), tile_m (CTAs of the persistent kernel, default the SM count),
+ * tile_k (percent of the entries handed out as claimed chunks, default 0),
+ * tile_n (pages per claimed chunk, default 4); flags: bit 0 CUDA-core
+ * consumer, bit 1 split-grid kernel instead of the persistent one, bit 2
+ * equal static ranges only. */
 size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq,
                                            int64_t max_blocks,
                                            int64_t block_size, int64_t D,
