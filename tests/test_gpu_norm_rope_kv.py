@@ -193,3 +193,36 @@ def test_fused_append_prefill_slot_owner_table(dtype, cuda_device):
         sm[1999] = sm[0]
         sm[7 + seed] = sm[900]         # token 900 wins over the earlier one
         _check_fused_append(cache, inp, cuda_device)
+
+
+@pytest.mark.parametrize("cfg_rows", [None, 2, 3, 6, 12])
+def test_fused_append_prefill_bench_shape(cfg_rows, cuda_device):
+    """The prefill-size append at the bench shape (16384 tokens, 32 q / 8 kv
+    heads, 48 rows per token -> the rows-per-thread kernel, two tokens per
+    CTA at the default), with collisions, invalid slots and out-of-table
+    positions, bit-exact against the oracle over the whole cache."""
+    cache = WL.paged_cache(num_blocks=16384, block_size=16, Hkv=8, D=128, device=cuda_device, seed=9)
+    inp = WL.decode_append_inputs(cache, n_tok=16384, Hq=32, device=cuda_device, seed=9)
+    sm, pos = inp["slot_mapping"], inp["positions"]
+    sm[5] = -1
+    sm[6] = 16384 * 16
+    sm[16383] = sm[100]            # the last token wins
+    sm[9000] = sm[8999]
+    pos[77] = -3                   # out of the cos/sin table: the token's rows stay untouched
+    cfg = {"rows_per_cta": cfg_rows} if cfg_rows else None
+    kc0, vc0 = cache.k_cache.clone(), cache.v_cache.clone()
+    q_out = K.rope_kv_append_paged(inp["q"], inp["k"], inp["v"], pos, inp["cos"], inp["sin"], sm,
+                                   cache.k_cache, cache.v_cache, cfg=cfg)
+    nslots = cache.num_blocks * cache.block_size
+    eq, ek, ev, keep = O.rope_kv_append_paged(inp["q"], inp["k"], inp["v"], pos, inp["cos"], inp["sin"], sm, nslots)
+    keep = keep.clone()
+    keep[77] = False               # its slot is unique, so the cache keeps the old row there
+    got_q = q_out.cpu()
+    ok_rows = (pos.cpu() >= 0)
+    assert torch.equal(got_q[ok_rows], eq[ok_rows])
+    sl = sm.cpu()[keep]
+    blk, off = sl // cache.block_size, sl % cache.block_size
+    kc0[blk.to(cuda_device), off.to(cuda_device)] = ek[keep].to(cuda_device)
+    vc0[blk.to(cuda_device), off.to(cuda_device)] = ev[keep].to(cuda_device)
+    assert torch.equal(cache.k_cache, kc0)
+    assert torch.equal(cache.v_cache, vc0)
