@@ -42,6 +42,10 @@ METRIC = "paged-decode tokens/s"
 DECODE_DRAM_BYTES_SMALL = 604_667_648 + 4_892_160
 DECODE_ALGO_BYTES_SMALL = 601_964_708  # printed by the same `bench.py --case decode` run
 UNIT = "tokens/s"
+# the decode follows the append on one stream and neither writes the other's
+# context lengths / block tables: programmatic dependent launch lets the
+# decode's prologue overlap the append's tail (b200_paged_attention cfg flags bit 3)
+DECODE_CFG = {"flags": 8}
 N_SEQ, HQ, HKV, D, BS, NBLK = 64, 32, 8, 128, 16, 65536
 WORKLOAD = {
     "workload": "decode step: fused RoPE+paged KV append (64 tok) then paged-attention decode",
@@ -306,7 +310,8 @@ def run_b200(args, ws, rank, local, dist):
     def step():
         K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"], app["sin"],
                                app["slot_mapping"], cache.k_cache, cache.v_cache, q_out=q_out)
-        K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"], out=out)
+        K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"], out=out,
+                          cfg=DECODE_CFG)
 
     for _ in range(args.warmup):
         step()
@@ -324,7 +329,8 @@ def run_b200(args, ws, rank, local, dist):
                                app["slot_mapping"], cache.k_cache, cache.v_cache, q_out=q_out)
 
     def decode_only():
-        K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"], out=out)
+        K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"], out=out,
+                          cfg=DECODE_CFG)
 
     def capture(fn):
         g = torch.cuda.CUDAGraph()
@@ -415,7 +421,8 @@ def run_b200(args, ws, rank, local, dist):
             stream.wait_event(ev["out_free"][k_])
         K.rope_kv_append_paged(x["app_q"], x["app_k"], x["app_v"], x["app_pos"], app["cos"], app["sin"],
                                x["app_slots"], cache.k_cache, cache.v_cache, q_out=q_out)
-        K.paged_attention(x["att_q"], cache.k_cache, cache.v_cache, x["att_table"], x["att_ctx"], out=out_buf[k_])
+        K.paged_attention(x["att_q"], cache.k_cache, cache.v_cache, x["att_table"], x["att_ctx"], out=out_buf[k_],
+                          cfg=DECODE_CFG)
         ev["in_free"][k_].record(stream)
         ev["out_ready"][k_].record(stream)
         with torch.cuda.stream(d2h_s):

@@ -201,7 +201,10 @@ int b200_rope_kv_append_paged_ws(const void* q, const void* k, const void* v,
  * tile_k (percent of the entries handed out as claimed chunks, default 0),
  * tile_n (pages per claimed chunk, default 4); flags: bit 0 CUDA-core
  * consumer, bit 1 split-grid kernel instead of the persistent one, bit 2
- * equal static ranges only. */
+ * equal static ranges only, bit 3 programmatic dependent launch (the
+ * kernel's prologue overlaps the previous kernel on the stream; the caller
+ * guarantees that kernel writes neither context_len nor block_table, as the
+ * decode-step append does not). */
 size_t b200_paged_attention_workspace_size(int64_t B, int64_t Hq,
                                            int64_t max_blocks,
                                            int64_t block_size, int64_t D,

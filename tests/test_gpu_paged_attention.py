@@ -155,3 +155,39 @@ def test_persistent_claimed_chunks(cfg, cuda_device):
     q2 = torch.randn(9, 32, 128, generator=g, device=cuda_device).bfloat16()
     out2 = run_and_check(q2, cache2.k_cache, cache2.v_cache, bt2, cl2, cuda_device, cfg=cfg)
     assert torch.count_nonzero(out2[5]) == 0
+
+
+def test_append_then_decode_with_programmatic_launch(cuda_device):
+    """Decode launched with programmatic dependent launch (flags bit 3)
+    right after the append, with no synchronisation between them, sees every
+    page the append wrote: bit-identical to append, synchronise, decode."""
+    cache = WL.paged_cache(num_blocks=16384, block_size=16, Hkv=8, D=128, device=cuda_device, seed=13)
+    att = WL.decode_attention_inputs(cache, B=64, Hq=32, ctx_lo=512, ctx_hi=4096, device=cuda_device, seed=13)
+    app = WL.decode_append_inputs(cache, n_tok=64, Hq=32, device=cuda_device, seed=13)
+    # every appended row lands in a page the decode reads (the first page of each sequence)
+    app["slot_mapping"] = (att["block_table"][:, 0].long() * 16 + 5).contiguous()
+    k0, v0 = cache.k_cache.clone(), cache.v_cache.clone()
+    q_out = torch.empty_like(app["q"])
+
+    def append():
+        K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"], app["sin"],
+                               app["slot_mapping"], cache.k_cache, cache.v_cache, q_out=q_out)
+
+    append()
+    torch.cuda.synchronize()
+    ref = K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"])
+    torch.cuda.synchronize()
+    for _ in range(3):
+        cache.k_cache.copy_(k0)
+        cache.v_cache.copy_(v0)
+        append()
+        out = K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"],
+                                cfg={"flags": 8})
+        torch.cuda.synchronize()
+        assert K.read_device_error() == 0
+        assert torch.equal(out, ref)
+    # the appended rows matter: without them the output differs
+    cache.k_cache.copy_(k0)
+    cache.v_cache.copy_(v0)
+    stale = K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"], att["context_len"])
+    assert not torch.equal(stale, ref)

@@ -946,6 +946,11 @@ __global__ void __launch_bounds__(288, 1)
     }
   }
   __syncthreads();
+  // With programmatic dependent launch (cfg flags bit 3) everything above
+  // (contexts, entry prefix, barriers) overlaps the previous kernel's tail;
+  // nothing below may read q or a KV page before that grid has completed and
+  // its writes are visible.  A no-op for an ordinary launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t E = s_cum[p.nseg];
   const int64_t Gc = gridDim.x;
   FlatRanges R;
@@ -1250,6 +1255,7 @@ struct Geometry {
   bool flat;  // persistent flat-partition kernel
   int flat_grid;
   int dyn_pct, chunk;  // persistent kernel: claimed share of the entries, entries per chunk
+  bool pdl;            // persistent kernel: programmatic dependent launch (flags bit 3)
   int64_t max_blocks_all;
   size_t flat_smem;
   int HG, n_hg, G, split_blocks, max_splits, stages;
@@ -1312,6 +1318,7 @@ Geometry choose_geometry(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t 
     g.dyn_pct = (cfg && (cfg->flags & 4)) ? 0 : (cfg && cfg->tile_k > 0 ? (cfg->tile_k < 90 ? cfg->tile_k : 90)
                                                                            : kFlatDynPct);
     g.chunk = (cfg && cfg->tile_n > 0) ? cfg->tile_n : kFlatChunk;
+    g.pdl = cfg && (cfg->flags & 8);
     const size_t extra = (size_t)g.stages * (2 * 8 + sizeof(PageMeta)) + (size_t)(nseg + 1) * 8 +
                          (size_t)B * 8 + 64 * 4 + 128 * 4 + 16 + (size_t)g.HG * g.G * 32 * 4;
     g.flat_smem = (size_t)g.stages * g.stage_bytes + extra + 1024;
@@ -1390,10 +1397,28 @@ int launch_tma(const void* q, const void* k_cache, const void* v_cache, const vo
     auto fk = paged_decode_flat_kernel<T, IDX, G>;
     cudaError_t e = cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)geo.flat_smem);
     if (e != cudaSuccess) return launch_status(e);
-    fk<<<geo.flat_grid, (geo.HG + 1) * 32, geo.flat_smem, stream>>>(
-        tk, tv, static_cast<const T*>(q), static_cast<const IDX*>(block_table), static_cast<const IDX*>(ctx_len),
-        static_cast<T*>(out), reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTicketBytes),
-        static_cast<int*>(workspace), fp);
+    // flags bit 3: programmatic dependent launch -- the prologue (context
+    // lengths, block-table prefix, barriers) may run while the previous
+    // kernel in the stream finishes; the kernel waits for that grid
+    // (griddepcontrol.wait) before its first q / KV read.  The caller
+    // guarantees the previous kernel writes neither context_len nor
+    // block_table (true for the decode-step append, which writes q_out and
+    // the cache).
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)geo.flat_grid);
+    lc.blockDim = dim3((unsigned)((geo.HG + 1) * 32));
+    lc.dynamicSmemBytes = geo.flat_smem;
+    lc.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = geo.pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&lc, fk, tk, tv, static_cast<const T*>(q), static_cast<const IDX*>(block_table),
+                           static_cast<const IDX*>(ctx_len), static_cast<T*>(out),
+                           reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTicketBytes),
+                           static_cast<int*>(workspace), fp);
+    if (e != cudaSuccess) return launch_status(e);
     return launch_status(cudaGetLastError());
   }
   auto kern = geo.mma ? paged_decode_kernel<T, IDX, G, true> : paged_decode_kernel<T, IDX, G, false>;

@@ -235,6 +235,10 @@ __global__ void __launch_bounds__(1024) rope_kv_append_paged_fast_kernel(
     const CS* __restrict__ sin, int64_t cs_rows, const int64_t* __restrict__ slots,
     T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t n_tok,
     int Hq, int Hkv, int64_t D, int64_t slot_hi, int tpr, int* __restrict__ owner) {
+  // a dependent kernel launched with programmatic stream serialisation (the
+  // paged decode) may start its prologue now; it waits for this grid's
+  // completion before it reads q_out or the cache
+  asm volatile("griddepcontrol.launch_dependents;");
   constexpr int VN = Vec<T>::N;
   const int64_t t = blockIdx.x;
   const int64_t half = D / 2;
