@@ -322,7 +322,11 @@ int b200_quantize_int8(const void* x, int8_t* q, float* scale, int64_t rows,
  * q: [B, H, T, D]; k, v: [B, H, S, D]; o: [B, H, T, D]; dtype F16/BF16;
  * D = 128 on the tensor-core path.  causal: mask key s > query t
  * (reference.py:25-28, which assumes T == S).  lse (nullable): [B, H, T] f32
- * natural-log softmax normaliser.  scale <= 0 means 1/sqrt(D). */
+ * natural-log softmax normaliser.  scale <= 0 means 1/sqrt(D).
+ * cfg: split (heads per scheduling group, default 8), tile_k (exponential
+ * pairs of every 8 computed by a polynomial on the FMA pipe: 1-3, default 2,
+ * 4 = none); flags: bit 4 persistent kernel, bit 2 two-tile kernel (bit 1
+ * with it: polynomial exponentials), bit 0 one-tile kernel. */
 int b200_flash_attn(const void* q, const void* k, const void* v, void* o,
                     float* lse, int64_t B, int64_t H, int64_t T, int64_t S,
                     int64_t D, float scale, int32_t causal, int32_t dtype,
