@@ -217,33 +217,31 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
         float* fi = row_f(r, i);
         if constexpr (!kF32) unpack16<T>(raw[r][i], fi);
         // quant_code_fast on pairs: q0 = RN(y r), e = y - q0 s, RN(q0 + e r) =
-        // RN(y / s); clamp to [-127, 127] first (the bounds are representable
-        // in T, and rounding is monotone, so clamp-then-round equals the
-        // reference's round-then-clamp), round the pair to T's precision with
-        // one packed conversion and widen it back, add 1.5 * 2^23 so the low
-        // byte of the bits is the two's-complement code of rint
-        uint32_t m[VN];
+        // RN(y / s); round the pair to T's precision with one packed
+        // conversion, add 1.5 * 2^23 so the low 16 bits of the bits are the
+        // integer rint as int16, clamp both codes to [-127, 127] with packed
+        // 16-bit integer min/max, and keep the low bytes
+        uint32_t h[VN / 2];
 #pragma unroll
         for (int j = 0; j < VN; j += 2) {
           float q0, q1, e0, e1, v0, v1;
           sm100::fmul2_bcast(q0, q1, fi[j], fi[j + 1], rs);
           sm100::ffma2(e0, e1, q0, q1, -s, -s, fi[j], fi[j + 1]);
           sm100::ffma2(v0, v1, e0, e1, rs, rs, q0, q1);
-          v0 = fmaxf(fminf(v0, 127.f), -127.f);
-          v1 = fmaxf(fminf(v1, 127.f), -127.f);
           round_pair_to<T>(v0, v1);
           sm100::ffma2_bcast(v0, v1, v0, v1, 1.0f, 12582912.0f);
-          m[j] = __float_as_uint(v0);
-          m[j + 1] = __float_as_uint(v1);
+          uint32_t p = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x5410);
+          asm("max.s16x2 %0, %1, %2;" : "=r"(p) : "r"(p), "r"(0xFF81FF81u));  // -127, -127
+          asm("min.s16x2 %0, %1, %2;" : "=r"(p) : "r"(p), "r"(0x007F007Fu));  // 127, 127
+          h[j / 2] = p;
         }
         if constexpr (VN == 8) {
           uint2 pk;
-          pk.x = __byte_perm(__byte_perm(m[0], m[1], 0x0040), __byte_perm(m[2], m[3], 0x0040), 0x5410);
-          pk.y = __byte_perm(__byte_perm(m[4], m[5], 0x0040), __byte_perm(m[6], m[7], 0x0040), 0x5410);
+          pk.x = __byte_perm(h[0], h[1], 0x6420);
+          pk.y = __byte_perm(h[2], h[3], 0x6420);
           *reinterpret_cast<uint2*>(qr + (int64_t)v * VN) = pk;
         } else {
-          const uint32_t pk = __byte_perm(__byte_perm(m[0], m[1], 0x0040), __byte_perm(m[2], m[3], 0x0040), 0x5410);
-          *reinterpret_cast<uint32_t*>(qr + (int64_t)v * VN) = pk;
+          *reinterpret_cast<uint32_t*>(qr + (int64_t)v * VN) = __byte_perm(h[0], h[1], 0x6420);
         }
       }
     }
