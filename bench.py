@@ -35,11 +35,11 @@ METRIC = "paged-decode tokens/s"
 # DRAM bytes (read + write) per algorithmic byte of the paged-decode kernel,
 # from one ncu capture of `bench.py --case decode` (16384-block cache, 64
 # sequences, ctx U[512,4096]; summary in profiles/paged_decode_flat_small.md):
-# 609.56 MB of DRAM traffic for the launch's algorithmic bytes.  The full
+# 609.92 MB of DRAM traffic for the launch's algorithmic bytes.  The full
 # launch (ctx U[512,8192], 65536 blocks) is too large for a full-set capture;
 # its traffic is this ratio times its algorithmic bytes (both grow with the
 # pages read).
-DECODE_DRAM_BYTES_SMALL = 604_667_648 + 4_892_160
+DECODE_DRAM_BYTES_SMALL = 604_623_872 + 5_299_712
 DECODE_ALGO_BYTES_SMALL = 601_964_708  # printed by the same `bench.py --case decode` run
 UNIT = "tokens/s"
 # the decode follows the append on one stream and neither writes the other's
