@@ -16,8 +16,9 @@ from __future__ import annotations
 import json
 import sqlite3
 import time
+from contextlib import contextmanager
 from pathlib import Path
-from typing import Any
+from typing import Any, Iterator
 
 from .spec import CandidateResult, OpAction, OpState
 
@@ -65,9 +66,20 @@ class LeaderboardStore:
         self.db_path = Path(db_path)
         self.db_path.parent.mkdir(parents=True, exist_ok=True)
         cols = ",\n".join(f"{n} {t}" for n, t in _COLUMNS)
-        with sqlite3.connect(str(self.db_path)) as conn:
+        with self._conn() as conn:
             conn.execute(f"CREATE TABLE IF NOT EXISTS leaderboard (id INTEGER PRIMARY KEY AUTOINCREMENT, {cols}, "
                          f"UNIQUE({', '.join(_KEY)}))")
+
+    @contextmanager
+    def _conn(self) -> Iterator[sqlite3.Connection]:
+        """One connection per operation: committed on success, rolled back on
+        error, closed either way."""
+        conn = sqlite3.connect(str(self.db_path))
+        try:
+            with conn:
+                yield conn
+        finally:
+            conn.close()
 
     def upsert(self, op_name: str, shape: str, dtype: str, device: str, action: OpAction, result: CandidateResult,
                episode_id: str) -> None:
@@ -86,7 +98,7 @@ class LeaderboardStore:
         updates = ", ".join(f"{n}=excluded.{n}" for n in names if n not in _KEY)
         sql = (f"INSERT INTO leaderboard ({', '.join(names)}) VALUES ({', '.join('?' for _ in names)}) "
                f"ON CONFLICT({', '.join(_KEY)}) DO UPDATE SET {updates}")
-        with sqlite3.connect(str(self.db_path)) as conn:
+        with self._conn() as conn:
             conn.execute(sql, [row[n] for n in names])
 
     def query(self, op_name: str, shape: str | None = None, dtype: str | None = None, limit: int = 20) -> list[dict]:
@@ -97,7 +109,7 @@ class LeaderboardStore:
         if dtype:
             where.append("dtype = ?")
             params.append(dtype)
-        with sqlite3.connect(str(self.db_path)) as conn:
+        with self._conn() as conn:
             conn.row_factory = sqlite3.Row
             rows = conn.execute(f"SELECT * FROM leaderboard WHERE {' AND '.join(where)} "
                                 f"ORDER BY speedup DESC LIMIT ?", params + [limit]).fetchall()
