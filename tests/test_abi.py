@@ -90,3 +90,23 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(L.B200OpsError) as ei:
         K.rmsnorm(torch.randn(2, 8), torch.randn(8))
     assert ei.value.code == L.ERR_NO_DEVICE
+
+
+def test_decode_workspace_sizes_for_claimed_chunks():
+    """Claimed chunks (cfg tile_k percent) need partial rows per chunk, so the
+    workspace query grows with the percent and shrinks with the chunk size;
+    the default (no claimed chunks) and equal ranges only (flags bit 2) ask
+    for the same bytes, within the 16 MiB scratch of the allocation-free
+    entry point at the bench shape (64 sequences, 32 heads, 512 blocks)."""
+    lib = L.load()
+
+    def ws(**kw):
+        cfg = L.LaunchCfg(**kw) if kw else None
+        return lib.b200_paged_attention_workspace_size(64, 32, 512, 16, 128, ctypes.byref(cfg) if cfg else None)
+
+    base = ws()
+    assert ws(flags=4) == base
+    assert ws(tile_k=25) > base
+    assert ws(tile_k=50) >= ws(tile_k=25)
+    assert ws(tile_k=25, tile_n=16) <= ws(tile_k=25, tile_n=4)
+    assert base <= 16 << 20
