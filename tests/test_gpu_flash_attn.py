@@ -1,5 +1,5 @@
 """GPU parity: tcgen05 flash-attention prefill vs the oracle (fp32), within
-2e-2 absolute (BASELINE), causal and full, bf16 and fp16, tails and both
+2e-2 absolute against fp32, causal and full, bf16 and fp16, tails and both
 head dims of the tensor-core path, plus the generic fallback."""
 
 import pytest

@@ -63,7 +63,7 @@ def test_int8_gemm_pair_kernel_tails(M, N, K_, cuda_device):
 
 
 def test_int8_gemm_baseline_shapes_checksum(cuda_device):
-    """Full BASELINE shapes: exact integer checks that do not need a full
+    """Full-size shapes (4096 x 4096, 4096 x 14336 and 16 x 14336, K = 4096): exact integer checks that do not need a full
     CPU GEMM -- column sums of the accumulator equal (1^T A) W^T and row sums
     equal A (W^T 1), both in int64, plus a sampled block compared exactly."""
     for M, N in [(4096, 4096), (4096, 14336), (16, 14336)]:

@@ -2,7 +2,7 @@
 the reference's golden outputs.
 
 Bars: cache writes, copies and fp32 RoPE are bit-exact; rmsnorm within
-1e-5 (fp32) / 1e-2 relative (bf16, fp16), the BASELINE tolerance.
+1e-5 (fp32) / 1e-2 relative (bf16, fp16), the stated tolerance.
 """
 
 import pytest

@@ -1,5 +1,5 @@
 """GPU parity: paged-attention decode vs the oracle (fp32) and the
-reference's golden outputs.  Tolerance: 2e-2 absolute (BASELINE), checked
+reference's golden outputs.  Tolerance: 2e-2 absolute against fp32, checked
 on every output element."""
 
 import math

@@ -4,7 +4,7 @@ Fixtures in tests/golden/ were produced by running the reference project's
 operator references (tests/golden/make_golden.py).  Tolerances: fp32 cases
 agree to rounding (1e-5); bf16/fp16 cases differ by the reference's
 per-operation half-precision rounding versus the oracle's single final
-rounding, bounded by 1e-2 relative (the BASELINE tolerance for
+rounding, bounded by 1e-2 relative (the stated tolerance for
 rmsnorm/RoPE).  Cache writes and int8 codes are compared exactly.
 """
 
