@@ -2,7 +2,7 @@
 
 This package restates, on the CPU, the algorithms of the reference project's
 PyTorch operator references (triton_agent/ops/<op>/reference.py).  It is the
-checker for the CUDA library: only tests/, __graft_entry__.smoke() and the
+parity oracle for the CUDA library: only tests/, __graft_entry__.smoke() and the
 cpu_baseline leg of bench.py may import it.  Nothing in the product package
 (triton-agent_b200/b200ops) imports or calls it, and the product never falls
 back to it.
