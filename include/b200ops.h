@@ -74,9 +74,15 @@ const char* b200_kernel_list(void);
  * injected-error note), or "" if none. */
 const char* b200_last_error_detail(void);
 /* Copies the per-library device error word (set by bounded waits that gave
- * up, or by checked index paths) into *out and clears it.  Synchronises the
- * given stream. */
+ * up: 1-4 waits inside a CTA, 6 a cross-GPU flag wait) into *out and clears
+ * it.  Synchronises the given stream. */
 int b200_read_device_error(int32_t* out, void* stream);
+/* Limit, in microseconds of GPU global time, of the cross-GPU flag waits of
+ * b200_int8_gemm_allgather (0 restores the default of 2 s).  Process-wide;
+ * read at each launch.  A wait that runs out records code 6 in the device
+ * error word and its kernel returns.  No counterpart in the reference (it has
+ * no multi-GPU path). */
+int b200_set_peer_wait_timeout_us(int64_t us);
 
 /* ---- rmsnorm ------------------------------------------------------------
  * Replaces triton_agent/ops/rmsnorm/reference.py:6-18
@@ -281,12 +287,19 @@ int b200_gemm_bias_gelu(const void* a, const void* b, const void* bias, void* c,
  * (the b200_int8_gemm formula) and writes it into C_ranks[r] for every rank
  * r < world (device pointers valid on this device: peers' buffers opened
  * with b200_ipc_open, this rank's own at index `rank`; all with the same
- * ldc).  It then stores `epoch` into sig_ranks[r][rank] for every r and
- * waits -- bounded, B200_ERR_DEVICE_TIMEOUT in the device error word on
- * expiry -- until sig_ranks[rank][r] >= epoch for every r, i.e. until every
- * rank's columns have landed in this rank's C.  sig arrays: `world` uint32
- * each, zero before the first call; epoch: strictly increasing per call.
- * All ranks must call it with the same M, K, epoch and world. */
+ * ldc).  Two flag exchanges bracket the GEMM, each bounded by
+ * b200_set_peer_wait_timeout_us (code 6 in the device error word on expiry):
+ *   - before it, this rank stores `epoch` into sig_ranks[r][world + rank] and
+ *     waits until sig_ranks[rank][world + r] >= epoch for every r: no rank
+ *     writes into a peer's C until that peer's stream has reached this call,
+ *     i.e. finished everything it ran before it, including its reads of the
+ *     previous call's C;
+ *   - after it, this rank stores `epoch` into sig_ranks[r][rank] and waits
+ *     until sig_ranks[rank][r] >= epoch for every r: every rank's columns
+ *     have landed in this rank's C.
+ * sig arrays: 2 * world uint32 each, zero before the first call; epoch:
+ * strictly increasing per call.  All ranks must call it with the same M, K,
+ * epoch and world. */
 int b200_int8_gemm_allgather(const int8_t* A, const int8_t* W_local, const float* sA,
                              const float* sW_local, void* const* C_ranks,
                              uint32_t* const* sig_ranks, int32_t world, int32_t rank,

@@ -59,6 +59,21 @@ def _worker(rank, world, port, q):
             Cf = fused(A, W[n0:n1].contiguous(), sA, sW[n0:n1].contiguous())
             torch.cuda.synchronize()
             gemm_ok = gemm_ok and bool(torch.equal(Cf, full))
+        # a rank still reading the previous result is not overwritten: rank 0
+        # holds its stream for a while before the next call and then snapshots
+        # C; the peers' next call (different scales) must not have landed yet
+        sA_b = (sA * 2).contiguous()
+        full_b = K.int8_gemm(A, W, sA_b, sW)
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            torch.cuda._sleep(200_000_000)  # ~0.1 s of device time
+            snap = fused.C.clone()
+        Cb = fused(A, W[n0:n1].contiguous(), sA_b, sW[n0:n1].contiguous())
+        torch.cuda.synchronize()
+        gemm_ok = gemm_ok and bool(torch.equal(Cb, full_b)) and K.read_device_error(dev) == 0
+        if rank == 0:
+            gemm_ok = gemm_ok and bool(torch.equal(snap, full))
         fused.close()
         A2, W2, sA2, sW2 = WL.int8_gemm_inputs(40, 1000, 256, device=dev, seed=7)
         full2 = K.int8_gemm(A2, W2, sA2, sW2)

@@ -47,11 +47,15 @@ def test_golden_reference_cases(golden_dir, cuda_device):
         torch.testing.assert_close(out.cpu().float(), c["out"], rtol=0, atol=ATOL)
 
 
-def test_baseline_config_sampled(cuda_device):
+def test_baseline_config_every_row(cuda_device):
+    """The full decode config (64 sequences, ctx U[512,8192], 65536-block
+    cache): every output row against the fp32 oracle, for the default
+    persistent kernel and the programmatic-launch flag the decode step uses."""
     cache = WL.paged_cache(device=cuda_device)
     inp = WL.decode_attention_inputs(cache, device=cuda_device)
-    run_and_check(inp["q"], cache.k_cache, cache.v_cache, inp["block_table"], inp["context_len"], cuda_device,
-                  sample=[0, 1, 7, 31, 63])
+    for cfg in (None, {"flags": 8}):
+        run_and_check(inp["q"], cache.k_cache, cache.v_cache, inp["block_table"], inp["context_len"], cuda_device,
+                      cfg=cfg)
 
 
 def test_baseline_config_all_rows_vs_single_split(cuda_device):

@@ -51,10 +51,14 @@ class FusedAllGatherGemm:
     per-call flags with the peers -- no collective call, no placement copy.
 
     Construction (collective over `group`): every rank allocates its full C
-    [M, N] and a `world`-entry uint32 flag array, shares CUDA IPC handles of
-    both through one all_gather_object and maps its peers'.  Each call
-    returns this object's C, which the next call overwrites.  W_local/sW_local
-    are this rank's rows [n0, n1) of W (column_shard(N, world, rank)).
+    [M, N] and a 2*world-entry uint32 flag array ("done" and "ready" flags),
+    shares CUDA IPC handles of both through one all_gather_object and maps its
+    peers'.  Each call returns this object's C, which the next call
+    overwrites.  A call first exchanges "ready" flags with every peer, so no
+    rank writes into a peer's C before that peer's stream has reached the
+    call (and so finished its reads of the previous result); then the GEMM;
+    then "done" flags, so the returned C is complete.  W_local/sW_local are
+    this rank's rows [n0, n1) of W (column_shard(N, world, rank)).
     """
 
     def __init__(self, M: int, N: int, out_dtype=torch.float16, device=None, group=None):
@@ -73,7 +77,7 @@ class FusedAllGatherGemm:
         self.col0, n1 = column_shard(N, self.world, self.rank)
         self.n_local = n1 - self.col0
         self.C = torch.empty(M, N, dtype=out_dtype, device=dev)
-        self.sig = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.sig = torch.zeros(2 * self.world, dtype=torch.int32, device=dev)
         lib = L.load()
         mine = []
         for t in (self.C, self.sig):

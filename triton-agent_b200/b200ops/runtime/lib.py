@@ -79,6 +79,7 @@ SIGNATURES = {
     "b200_kernel_list": (c_char_p, []),
     "b200_last_error_detail": (c_char_p, []),
     "b200_read_device_error": (c_int, [POINTER(c_int32), P]),
+    "b200_set_peer_wait_timeout_us": (c_int, [I64_]),
     "b200_rmsnorm": (c_int, [P, P, P, I64_, I64_, c_float, c_int32, c_int32, PCFG, P]),
     "b200_rmsnorm_quant_int8": (c_int, [P, P, P, P, P, I64_, I64_, c_float, c_int32, c_int32, PCFG, P]),
     "b200_rope": (c_int, [P, P, P, P, I64_, I64_, I64_, I64_, c_int32, c_int32, PCFG, P]),

@@ -343,8 +343,18 @@ def flash_attn(q, k, v, causal: bool = False, scale: float | None = None, out=No
     return o
 
 
+# device error word codes (first failure wins)
+DEV_ERR_TIMEOUT_FULL, DEV_ERR_TIMEOUT_EMPTY, DEV_ERR_TIMEOUT_MMA, DEV_ERR_TIMEOUT_COMBINE = 1, 2, 3, 4
+DEV_ERR_TIMEOUT_PEER = 6
+
+
+def set_peer_wait_timeout_us(us: int) -> None:
+    """Limit of the cross-GPU flag waits of the fused all-gather GEMM (0 = 2 s)."""
+    L.check(L.load().b200_set_peer_wait_timeout_us(int(us)), "set_peer_wait_timeout_us")
+
+
 def read_device_error(device: torch.device | None = None) -> int:
-    """Device error word set by bounded waits / checked paths (0 = none)."""
+    """Device error word set by bounded waits that gave up (0 = none; codes above)."""
     dev = device or torch.device("cuda", torch.cuda.current_device())
     v = ctypes.c_int32(0)
     L.check(L.load().b200_read_device_error(ctypes.byref(v), _stream(dev)), "read_device_error")

@@ -66,8 +66,13 @@ enum DeviceError : int {
   kDevErrTimeoutEmpty = 2,    // producer gave up waiting for a free stage
   kDevErrTimeoutMma = 3,      // epilogue gave up waiting for the accumulator
   kDevErrTimeoutCombine = 4,  // combine step gave up waiting for partials
-  kDevErrBounds = 5,          // checked index path found an out-of-range index
+  kDevErrTimeoutPeer = 6,     // a cross-GPU flag wait gave up waiting for a peer rank
 };
+
+// Limit of the cross-GPU flag waits (fused all-gather GEMM), in ns of global
+// time: b200_set_peer_wait_timeout_us, default 2 s.  The mbarrier waits
+// inside a CTA keep their fixed 2 s limit.
+uint64_t peer_wait_timeout_ns();
 
 }  // namespace b200
 

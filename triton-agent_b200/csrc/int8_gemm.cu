@@ -1210,22 +1210,30 @@ int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* s
   }
 }
 
-// After a fused all-gather GEMM on the same stream: thread r tells rank r
-// that this rank's columns are in r's C (release store at system scope),
-// then waits (bounded) for rank r's flag in this rank's array.
-__global__ void __launch_bounds__(32) peer_signal_wait_kernel(Gather flags, int world, int self, uint32_t epoch) {
+// Cross-GPU flag exchange of the fused all-gather GEMM.  Each rank's flag
+// array holds 2 * world uint32: entries [0, world) are "done" flags (rank r's
+// columns of this call are in my C) and entries [world, 2 * world) are
+// "ready" flags (rank r has reached this call, so everything its stream ran
+// before it -- including its reads of the previous call's C -- is finished).
+// Thread r stores `epoch` into rank r's array at index base + self (release
+// store at system scope), then waits, bounded by `timeout_ns` of global time,
+// until entry base + r of this rank's own array has reached `epoch`.  On
+// expiry it records `err_code` in the device error word and returns.
+__global__ void __launch_bounds__(32) peer_flag_exchange_kernel(Gather flags, int world, int self, int base,
+                                                                 uint32_t epoch, uint64_t timeout_ns,
+                                                                 int err_code) {
   const int r = threadIdx.x;
   if (r >= world) return;
-  uint32_t* mine = static_cast<uint32_t*>(flags.dst[self]);
-  uint32_t* theirs = static_cast<uint32_t*>(flags.dst[r]);
+  uint32_t* mine = static_cast<uint32_t*>(flags.dst[self]) + base;
+  uint32_t* theirs = static_cast<uint32_t*>(flags.dst[r]) + base;
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(theirs + self), "r"(epoch) : "memory");
   const uint64_t t0 = sm100::global_timer_ns();
   while (true) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
     if ((int32_t)(v - epoch) >= 0) break;
-    if (sm100::global_timer_ns() - t0 > sm100::kWaitTimeoutNs) {
-      b200_dev_error(kDevErrTimeoutCombine);
+    if (sm100::global_timer_ns() - t0 > timeout_ns) {
+      b200_dev_error(err_code);
       break;
     }
     __nanosleep(64);
@@ -1267,12 +1275,19 @@ extern "C" int b200_int8_gemm_allgather(const int8_t* A, const int8_t* W_local, 
   // runs the persistent one-SM kernel (flags bit 0) instead of the swap-AB ones
   b200_launch_cfg c = cfg ? *cfg : b200_launch_cfg{};
   c.flags |= 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t timeout_ns = peer_wait_timeout_ns();
+  // Nobody writes into a peer's C before that peer has reached this call: its
+  // stream has then finished whatever read the previous call's result.
+  peer_flag_exchange_kernel<<<1, 32, 0, s>>>(fl, world, rank, world, epoch, timeout_ns, kDevErrTimeoutPeer);
+  if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return launch_status(e);
   if (M > 0 && n_local > 0) {
     const int st = gemm_entry(A, W_local, sA, sW_local, C_ranks[rank], M, n_local, K, ldc, out_dtype, nullptr,
                               workspace, workspace_bytes, &c, stream, ga);
     if (st != B200_OK) return st;
   }
-  peer_signal_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, world, rank, epoch);
+  // Every rank's columns have landed in this rank's C when this one returns.
+  peer_flag_exchange_kernel<<<1, 32, 0, s>>>(fl, world, rank, 0, epoch, timeout_ns, kDevErrTimeoutPeer);
   return launch_status(cudaGetLastError());
 }
 

@@ -1617,8 +1617,11 @@ extern "C" int b200_paged_attention_noalloc(const void* q, const void* k_cache, 
   if (B == 0) return B200_OK;
   void* scratch = nullptr;
   if (int st = noalloc_scratch(&scratch)) return st;
-  // Ticket counters (one int per sequence x kv head at most) start at zero.
-  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)B * Hkv * sizeof(int), static_cast<cudaStream_t>(stream));
+  // The whole ticket region starts at zero: the per-(sequence, head group)
+  // merge tickets at its start and the claimed-chunk pool counters at its end.
+  // Both re-arm themselves when a launch completes, but a launch whose bounded
+  // wait gave up can leave them stale in this shared array; 256 KB is cheap.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, b200::kTicketBytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return b200::launch_status(e);
   return b200_paged_attention(q, k_cache, v_cache, block_table, context_len, out, B, Hq, Hkv, D, num_blocks,
                               block_size, max_blocks, scale, dtype, index_dtype, scratch, kNoAllocScratchBytes,

@@ -4,6 +4,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -54,6 +55,12 @@ int launch_status(cudaError_t e) {
   set_last_error_detail(cudaGetErrorString(e));
   return B200_ERR_LAUNCH;
 }
+
+namespace {
+std::atomic<uint64_t> g_peer_wait_timeout_ns{sm100::kWaitTimeoutNs};
+}  // namespace
+
+uint64_t peer_wait_timeout_ns() { return g_peer_wait_timeout_ns.load(std::memory_order_relaxed); }
 
 int injected_error(const char* op_name) {
   const char* v = getenv("B200OPS_INJECT_ERROR");
@@ -144,7 +151,7 @@ const char* b200_kernel_list(void) {
          "int8_gemm_tcgen05_kernel\n"
          "int8_gemm_stream_kernel\n"
          "int8_gemm_skinny_kernel\n"
-         "peer_signal_wait_kernel\n"
+         "peer_flag_exchange_kernel\n"
          "quantize_rows_kernel\n"
          "quantize_cols_kernel\n"
          "flash_fwd3_tcgen05_kernel\n"
@@ -212,6 +219,13 @@ int b200_ipc_close(void* dev_ptr, int64_t offset) {
     b200::set_last_error_detail(cudaGetErrorString(e));
     return B200_ERR_LAUNCH;
   }
+  return B200_OK;
+}
+
+int b200_set_peer_wait_timeout_us(int64_t us) {
+  if (us < 0) return B200_ERR_BAD_ARG;
+  b200::g_peer_wait_timeout_ns.store(us == 0 ? b200::sm100::kWaitTimeoutNs : (uint64_t)us * 1000ull,
+                                     std::memory_order_relaxed);
   return B200_OK;
 }
 
