@@ -34,7 +34,7 @@ import torch  # noqa: E402
 METRIC = "paged-decode tokens/s"
 # DRAM bytes (read + write) per algorithmic byte of the paged-decode kernel,
 # from one ncu capture of `bench.py --case decode` (16384-block cache, 64
-# sequences, ctx U[512,4096]; summary in profiles/paged_decode_flat_small.md):
+# sequences, ctx U[512,4096]):
 # 609.92 MB of DRAM traffic for the launch's algorithmic bytes.  The full
 # launch (ctx U[512,8192], 65536 blocks) is too large for a full-set capture;
 # its traffic is this ratio times its algorithmic bytes (both grow with the
@@ -81,6 +81,24 @@ def max_over_ranks(dist, v: float, device) -> float:
     t = torch.tensor([v], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_per_rank(dist, device, ws, **vals) -> dict:
+    """Each named figure from every rank (rank order), with its max/min
+    spread: which rank limits a weak-scaled step and whether its clock did."""
+    if dist is None or ws == 1:
+        return {k: [v] for k, v in vals.items()}
+    t = torch.tensor([float(v) for v in vals.values()], dtype=torch.float64, device=device)
+    out = [torch.empty_like(t) for _ in range(ws)]
+    dist.all_gather(out, t)
+    cols = torch.stack(out).cpu()
+    res = {}
+    for i, k in enumerate(vals):
+        col = [float(x) for x in cols[:, i]]
+        res[k] = col
+        if min(col) > 0:
+            res[f"{k}_spread"] = max(col) / min(col)
+    return res
 
 
 def barrier(dist):
@@ -272,8 +290,18 @@ def sharded_gemm(dev, dist, ws) -> dict:
         return max_over_ranks(dist, e0.elapsed_time(e1) * 1e3 / reps, dev)
 
     ops = 2 * M * N * Kd
-    us_nccl = timed(lambda: sharded_int8_gemm(A, Wl, sA, sWl, N, gemm))
+    # both multi-GPU results equal the one-GPU GEMM bit for bit before either is timed
+    full = K.int8_gemm(A, W, sA, sW)
+    exact_nccl = bool(torch.equal(sharded_int8_gemm(A, Wl, sA, sWl, N, gemm), full))
     fused = FusedAllGatherGemm(M, N, device=dev)
+    exact_fused = bool(torch.equal(fused(A, Wl, sA, sWl).clone(), full))
+    torch.cuda.synchronize()
+    exact = max_over_ranks(dist, 0.0 if (exact_nccl and exact_fused and K.read_device_error(dev) == 0) else 1.0,
+                           dev) == 0.0
+    if not exact:
+        raise RuntimeError("sharded INT8 GEMM differs from the one-GPU GEMM on some rank")
+    del full
+    us_nccl = timed(lambda: sharded_int8_gemm(A, Wl, sA, sWl, N, gemm))
     us_fused = timed(lambda: fused(A, Wl, sA, sWl))
     fused.close()
     peaks = measured_peaks()
@@ -282,11 +310,12 @@ def sharded_gemm(dev, dist, ws) -> dict:
     target_us = max(ops / ws / (2 * peaks["bf16_tflops"]) / 1e6, sent / link_gbs / 1e3)
     return {
         f"int8_gemm_colsharded_M{M}_N{N}_K{Kd}_x{ws}": {
-            "us": us_nccl, "TOPS_total": ops / us_nccl / 1e6, "includes": "local GEMM + NCCL all-gather + placement"},
+            "us": us_nccl, "TOPS_total": ops / us_nccl / 1e6, "bit_exact_vs_1gpu": exact_nccl,
+            "includes": "local GEMM + NCCL all-gather + placement"},
         f"int8_gemm_allgather_fused_M{M}_N{N}_K{Kd}_x{ws}": {
             "us": us_fused, "TOPS_total": ops / us_fused / 1e6, "nvlink_bytes_sent_per_rank": sent,
-            "roofline_us": target_us, "frac": target_us / us_fused,
-            "includes": "GEMM with peer-store epilogue + flag exchange"},
+            "roofline_us": target_us, "frac": target_us / us_fused, "bit_exact_vs_1gpu": exact_fused,
+            "includes": "ready-flag exchange + GEMM with peer-store epilogue + done-flag exchange"},
     }
 
 
@@ -323,6 +352,7 @@ def run_b200(args, ws, rank, local, dist):
     # come from two more graphs of n appends and n decodes timed the same
     # way.  If capture is refused, the same loop runs eagerly.
     n = args.steps
+    peaks = measured_peaks()
 
     def append_only():
         K.rope_kv_append_paged(app["q"], app["k"], app["v"], app["positions"], app["cos"], app["sin"],
@@ -368,9 +398,14 @@ def run_b200(args, ws, rank, local, dist):
     with ClockSampler(local) as clk:
         ms_local = timed(0)
     ms = max_over_ranks(dist, ms_local, dev)
-    append_ms = max_over_ranks(dist, timed(1), dev) / n
-    decode_ms = max_over_ranks(dist, timed(2), dev) / n
+    append_local = timed(1) / n
+    decode_local = timed(2) / n
+    append_ms = max_over_ranks(dist, append_local, dev)
+    decode_ms = max_over_ranks(dist, decode_local, dev)
     clocks = clk.summary()
+    per_rank = gather_per_rank(dist, dev, ws, step_ms=ms_local / n, decode_ms=decode_local,
+                               append_ms=append_local, sm_mhz=clocks.get("sm_mhz") or 0.0,
+                               decode_gbps=WL.decode_bytes(att["context_len"], HQ, HKV, D, BS) / decode_local / 1e6)
     assert K.read_device_error(dev) == 0, "device error word set during the timed region"
     graphs = None  # release the graphs before the process group goes
 
@@ -451,14 +486,14 @@ def run_b200(args, ws, rank, local, dist):
 
     tokens = N_SEQ * ws * n
     value = tokens / (ms / 1e3)
-    peaks = measured_peaks()
     dec_bytes = WL.decode_bytes(att["context_len"], HQ, HKV, D, BS, index_bytes=4)
     achieved = dec_bytes / (decode_ms / 1e3) / 1e9
     traffic = DECODE_DRAM_BYTES_SMALL / DECODE_ALGO_BYTES_SMALL * dec_bytes if DECODE_ALGO_BYTES_SMALL else None
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": n, "warmup": args.warmup,
         "ms_per_step": ms / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded, on device)", "config": {**WORKLOAD, "parallelism": f"dp{ws} (sequences)"},
+        "dtype": "bf16", "data": "synthetic (seeded, on device)", "config": dict(WORKLOAD),
+        "parallelism": f"dp{ws} (sequences; each rank owns its sequences' KV pages, no collective)",
         "e2e": {"value": N_SEQ * ws * n / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / n,
                 "pipeline": "inputs packed into one pinned buffer, host->device copy of step i+1 on a copy "
@@ -470,6 +505,13 @@ def run_b200(args, ws, rank, local, dist):
                      "algorithmic_bytes_per_launch": dec_bytes,
                      "kernel_ms": decode_ms},
         "per_op_ms": {"rope_kv_append_paged": append_ms, "paged_attention": decode_ms}, "timing": timing,
+        "decode_step_append": {
+            "what": "the step's fused RoPE + paged append of 64 new tokens alone (n appends in one graph)",
+            "us": append_ms * 1e3, "tokens_per_s": N_SEQ * ws / (append_ms / 1e3),
+            "GBps": WL.append_bytes(N_SEQ, HQ, HKV, D) / append_ms / 1e6,
+            "frac": WL.append_bytes(N_SEQ, HQ, HKV, D) / append_ms / 1e6 / peaks["hbm_gbs"],
+            "algorithmic_bytes": WL.append_bytes(N_SEQ, HQ, HKV, D), "bound": "launch/latency (1.6 MB per call)"},
+        **({"per_rank": per_rank} if ws > 1 else {}),
         "gpu_launches": 2 * n,
         "clocks": clocks,
     }
@@ -517,6 +559,21 @@ def cpu_decode_time(x: dict) -> float:
 CPU_SAMPLE_DESC = "decode step of {n} sequences (ctx U[512,8192]), oracle port"
 
 
+def cpu_clone_seconds(reps: int = 2) -> float:
+    """Seconds per step of the reference's functional append semantics: its
+    paged append returns modified copies of both caches
+    (paged_kv/reference.py:15-16, kv_append/reference.py:30-31), i.e. one
+    clone of each [65536, 16, 8, 128] bf16 cache (2 GiB each) per step."""
+    kc = torch.empty(NBLK, BS, HKV, D, dtype=torch.bfloat16).fill_(1.0)
+    vc = torch.empty_like(kc).fill_(1.0)
+    kc.clone(), vc.clone()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        k2, v2 = kc.clone(), vc.clone()
+        del k2, v2
+    return (time.perf_counter() - t0) / reps
+
+
 def run_reference(args, ws, rank):
     """Reference arm: the reference's CPU path (oracle port) on the host cores."""
     if rank != 0:
@@ -529,13 +586,20 @@ def run_reference(args, ws, rank):
     t_total = sum(cpu_decode_time(x) for _ in range(args.steps))
     desc = CPU_SAMPLE_DESC.format(n=sample)
     value = sample * args.steps / t_total
+    try:
+        clone_s = cpu_clone_seconds()
+        with_clone = {"value": sample / (t_total / args.steps + clone_s), "unit": UNIT, "clone_s_per_step": clone_s,
+                      "what": "the same step plus one clone of each 2 GiB cache (paged_kv/reference.py:15-16)"}
+    except RuntimeError as e:
+        with_clone = {"unavailable": str(e)[:120]}
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": WORKLOAD,
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": dict(WORKLOAD),
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": desc},
+                         "sample": desc + " (clone-free; the reference's per-append cache clones are timed in "
+                                          "with_reference_clone)", "with_reference_clone": with_clone},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -638,6 +702,15 @@ def main():
                 res["cpu_baseline"] = {"value": N_SEQ * i / secs, "unit": UNIT, "cores": torch.get_num_threads(),
                                        "kind": "port", "sample": f"{i} x " + CPU_SAMPLE_DESC.format(n=N_SEQ),
                                        "seconds": secs}
+                try:
+                    clone_s = cpu_clone_seconds()
+                    step_s = secs / i
+                    res["cpu_baseline"]["with_reference_clone"] = {
+                        "value": N_SEQ / (step_s + clone_s), "unit": UNIT, "clone_s_per_step": clone_s,
+                        "what": "the same step plus the reference's functional append: one clone of each 2 GiB "
+                                "cache per step (paged_kv/reference.py:15-16)"}
+                except RuntimeError as e:  # host memory: two 2 GiB caches and their clones
+                    res["cpu_baseline"]["with_reference_clone"] = {"unavailable": str(e)[:120]}
             print(json.dumps(res))
     finally:
         if dist is not None:

@@ -2,7 +2,8 @@
 operator references on small seeded inputs.
 
 Usage (in a container that has the reference checked out):
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
+    (or set TRITON_AGENT_REF to the checkout and omit --ref)
 
 Each reference.py is imported by file path (they depend only on torch and
 math), so no part of the reference package is installed or copied.  The
@@ -20,6 +21,7 @@ softmax) executes as written.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 from pathlib import Path
 
@@ -189,7 +191,9 @@ def make(ref_root: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    env = os.environ.get("TRITON_AGENT_REF")
+    ap.add_argument("--ref", default=env, required=env is None,
+                    help="root of a Triton-Agent checkout (default: $TRITON_AGENT_REF)")
     args = ap.parse_args()
     make(Path(args.ref))
 
