@@ -77,6 +77,19 @@ const char* b200_last_error_detail(void);
  * up: 1-4 waits inside a CTA, 6 a cross-GPU flag wait) into *out and clears
  * it.  Synchronises the given stream. */
 int b200_read_device_error(int32_t* out, void* stream);
+/* Tunable launch parameters of an op, as JSON text:
+ *   {"op": ..., "rows": ..., "kernel": <kernel the default dispatch selects>,
+ *    "sm_count": ..., "fields": {<b200_launch_cfg field>: {"values": [...],
+ *    "meaning": ...}, ...}}
+ * listing only the fields that kernel reads, each with the values it accepts
+ * (0 = the kernel's default).  `rows` selects the kernel where the op has
+ * several (quant_matmul: M <= 64 streaming, <= 128 one-SM, else CTA pairs;
+ * rope_kv_append_paged: tokens; 0 = the op's benchmark shape).  Op names are
+ * those of triton_agent/ops (the registry keys of core/registry.py); NULL for
+ * an unknown op.  The text stays valid until the next call on the same
+ * thread.  Replaces the Triton-config search space the reference's tuner
+ * reads from contract.yaml (core/contract.py:62-69, cli.py:281-293). */
+const char* b200_query_config_space(const char* op, int64_t rows);
 /* Limit, in microseconds of GPU global time, of the cross-GPU flag waits of
  * b200_int8_gemm_allgather (0 restores the default of 2 s).  Process-wide;
  * read at each launch.  A wait that runs out records code 6 in the device

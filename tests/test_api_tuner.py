@@ -28,10 +28,55 @@ def contract(op="paged_attention"):
 def test_grid_spans_cuda_axes():
     c = contract()
     grid = generate_grid(c, STATE, {"cuda_v1.sm100": None})
-    splits = {a.split for _, a in grid}
-    stages = {a.num_stages for _, a in grid}
-    assert splits == {8, 16, 32, 64} and stages == {2, 3}
+    assert {a.rows_per_cta for _, a in grid} == {0, 4} and {a.num_stages for _, a in grid} == {0, 3}
+    assert {a.tile_m for _, a in grid} == {0, 296} and {a.tile_k for _, a in grid} == {0, 10}
     assert len(grid) == len({a.arm_key() for _, a in grid})  # no duplicate launches
+
+
+ROWS = (0, 16, 100, 4096, 16384)
+
+
+@pytest.mark.parametrize("op", sorted(d.name for d in OPS_DIR.iterdir() if (d / "contract.yaml").exists()))
+def test_contract_axes_are_parameters_the_kernels_read(op):
+    """Every CUDA axis a contract searches is a b200_launch_cfg field that the
+    kernel the op selects (for some size) reads, and every value the contract
+    lists is one that kernel accepts -- the tuner never times a dead knob."""
+    from b200ops.runtime import lib as L
+
+    spaces = [L.config_space(op, r) for r in ROWS]
+    assert all(sp is not None and sp["op"] == op and sp["kernel"] for sp in spaces)
+    fields = {}
+    for sp in spaces:
+        for k, v in sp["fields"].items():
+            fields.setdefault(k, set()).update(v["values"])
+    for key, values in contract(op).search_space.cuda.items():
+        assert key in fields, (op, key, sorted(fields))
+        assert set(values) <= fields[key], (op, key, values, fields[key])
+        assert 0 in values, (op, key)  # the kernel's default is always an arm
+
+
+def test_axes_are_pruned_to_the_selected_kernel():
+    from b200ops.agent.generator import _axes, default_action, library_axes
+    from b200ops.runtime import lib as L
+
+    big = dict(_axes(contract("quant_matmul"), L.config_space("quant_matmul", 4096)))
+    assert big["tile_k"] == [0] and big["flags"] == [0, 2] and big["num_stages"] == [0, 4, 6, 8]
+    small = dict(_axes(contract("quant_matmul"), L.config_space("quant_matmul", 16)))
+    assert small["flags"] == [0] and small["tile_n"] == [0] and small["tile_k"] == [0, 256, 1024]
+    assert small["num_stages"] == [0, 4, 6, 8, 12] and small["num_warps"] == [0]
+    dec = dict(_axes(contract("paged_attention"), L.config_space("paged_attention", 64)))
+    assert dec.get("split", [0]) == [0] and dec["rows_per_cta"] == [0, 4] and dec["tile_m"] == [0, 296]
+    fl = dict(_axes(contract("flash_attn_like"), L.config_space("flash_attn_like", 0)))
+    assert fl["num_stages"] == [0] and fl["split"] == [0, 4, 16] and fl["flags"] == [0, 16]
+    # the default arm launches with an empty b200_launch_cfg
+    axes = _axes(contract("paged_attention"), L.config_space("paged_attention", 64))
+    d = default_action("cuda_v1.sm100", axes)
+    assert not any(d.launch_cfg().values())
+    assert d.arm_key() in {a.arm_key() for _, a in generate_grid(contract(), STATE, {"cuda_v1.sm100": None},
+                                                                   axes=axes)}
+    lib = dict(library_axes(L.config_space("flash_attn_like", 0)))
+    assert lib["tile_k"] == [0, 1, 2, 3, 4] and lib["num_stages"] == [0] and lib["num_warps"] == [0]
+    assert L.config_space("no_such_op") is None
 
 
 def test_best_of_n_is_seeded_and_planner_threshold():

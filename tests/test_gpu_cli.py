@@ -54,7 +54,7 @@ def test_optimize_records_a_verified_best(strategy, tmp_path):
     rec = json.loads(eps[0].read_text())
     assert rec["result"]["verify_pass"] and rec["result"]["latency_us_p50"] > 0
     assert len(rec["extra"]["candidates"]) == 4
-    assert {c["action"]["threads"] for c in rec["extra"]["candidates"]} <= {128, 256, 512, 1024}
+    assert {c["action"]["threads"] for c in rec["extra"]["candidates"]} <= {0, 128, 256, 512, 1024}
     assert (tmp_path / "leaderboard.sqlite").exists()
     # a second run warm-starts from the leaderboard's best and evaluates it first
     res = CliRunner().invoke(cli.main, ["optimize", "rmsnorm", "--shape", "B=4,T=256,D=4096", "--dtype", "bf16",
@@ -81,3 +81,48 @@ def test_bad_launch_config_becomes_a_failed_candidate():
     r = cli.evaluate("rmsnorm", contract, factory, OpAction("cuda_v1.sm100", threads=48), st, inputs,
                      ref_fn(*inputs))
     assert r.compile_pass and not r.verify_pass and "bad argument" in r.compile_log
+
+
+# The hot kernels' real launch parameters: the persistent decode (kv heads per
+# CTA, ring depth, grid, claimed chunks), the INT8 GEMM at a CTA-pair size and
+# at a streaming size, and the flash prefill (head groups, FMA-pipe
+# exponentials, persistent kernel).
+TUNE = [
+    ("paged_attention", "B=32,H=32,H_kv=8,D=128,num_blocks=4096,block_size=16,max_blocks=128,ctx_len=1800", "bf16"),
+    ("quant_matmul", "B=1,M=512,K=1024,N=2048", "fp16"),
+    ("quant_matmul", "B=1,M=16,K=4096,N=4096", "fp16"),
+    ("flash_attn_like", "B=1,H=8,T=1024,S=1024,D=128", "bf16"),
+]
+
+
+@pytest.mark.parametrize("op,shape,dtype", TUNE)
+def test_optimize_tunes_the_hot_kernels_launch_parameters(op, shape, dtype, tmp_path):
+    """optimize --strategy ucb measures the kernel's all-default launch and
+    other configurations of the parameters b200_query_config_space says the
+    selected kernel reads; every candidate passes the correctness gate and
+    the episode records the default beside the best."""
+    from b200ops.core.spec import CUDA_FIELDS
+
+    res = CliRunner().invoke(cli.main, ["optimize", op, "--shape", shape, "--dtype", dtype, "--strategy", "ucb",
+                                        "--max-candidates", "6", "--out", str(tmp_path)])
+    assert res.exit_code == 0, res.output
+    rec = json.loads(next((tmp_path / op).glob("*/record.json")).read_text())
+    extra = rec["extra"]
+    space = extra["config_space"]
+    assert space and space["op"] == op
+    reads = set(space["fields"])
+    cands = extra["candidates"]
+    assert len(cands) == 6 and all(c["result"]["verify_pass"] for c in cands), cands
+    cfgs = set()
+    for c in cands:
+        a = c["action"]
+        knobs = {f: a[f] for f in CUDA_FIELDS if a[f]}
+        if a["num_stages"]:
+            knobs["stages"] = a["num_stages"]
+        assert set(knobs) <= reads, (knobs, reads)  # no dead knob is ever timed
+        cfgs.add(tuple(sorted(knobs.items())))
+    assert len(cfgs) == 6  # six different launches
+    assert () in cfgs  # the kernel's defaults
+    d = extra["default"][0]["result"]
+    assert d["verify_pass"] and d["latency_us_p50"] > 0
+    assert rec["result"]["latency_us_p50"] > 0

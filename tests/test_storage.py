@@ -84,7 +84,9 @@ def _fake_eval(log):
     3 stages is the fastest configuration."""
     def ev(tid, action):
         log.append(action)
-        lat = 10.0 + (64 - action.split) / 8 + (3 - action.num_stages)
+        # best arm: 4 kv heads per CTA, two CTAs per SM, ring depth 3, no claimed chunks
+        lat = (10.0 + (0 if action.rows_per_cta == 4 else 2) + (0 if action.tile_m == 296 else 1)
+               + (0 if action.num_stages == 3 else 0.5) + action.tile_k / 10)
         r = CandidateResult(compile_pass=True, verify_pass=True, latency_us_p50=lat, speedup=12.0 / lat,
                             roofline_fraction=8.0 / lat)
         compute_score(r)
@@ -110,21 +112,23 @@ def _run(tmp_path, strategy, max_candidates, warm_start=True):
 
 
 def test_optimize_records_and_warm_starts(tmp_path):
-    log, action, best, path, ep = _run(tmp_path, "grid", 16)
-    assert len(log) == 8 and (action.split, action.num_stages) == (64, 3) and best.promoted
+    best_key = (4, 296, 3, 0)
+    key = lambda a: (a.rows_per_cta, a.tile_m, a.num_stages, a.tile_k)  # noqa: E731
+    log, action, best, path, ep = _run(tmp_path, "grid", 32)
+    assert len(log) == 16 and key(action) == best_key and best.promoted
     rec = json.loads((path / "record.json").read_text())
-    assert len(rec["extra"]["candidates"]) == 8 and rec["result"]["latency_us_p50"] == best.latency_us_p50
+    assert len(rec["extra"]["candidates"]) == 16 and rec["result"]["latency_us_p50"] == best.latency_us_p50
     row = LeaderboardStore(tmp_path / "leaderboard.sqlite").best_config("paged_attention", "B=64,Hq=32,D=128", "bf16")
-    assert row["episode_id"] == ep and row["split"] == 64 and abs(row["roofline_fraction"] - 0.8) < 1e-9
+    assert row["episode_id"] == ep and row["rows_per_cta"] == 4 and abs(row["roofline_fraction"] - 0.8) < 1e-9
 
-    # one candidate only: without a warm start the grid's first point (split 8)
+    # one candidate only: without a warm start the grid's first point (every default)
     log, action, _, _, _ = _run(tmp_path / "cold", "grid", 1, warm_start=False)
-    assert action.split == 8
+    assert key(action) == (0, 0, 0, 0)
     # with it, the stored best is evaluated first and stays the best
     for strategy in ("grid", "best_of_n", "ucb", "reinforce", "grpo"):
         log, action, _, _, _ = _run(tmp_path, strategy, 1)
-        assert (log[0].split, log[0].num_stages) == (64, 3), strategy
-        assert (action.split, action.num_stages) == (64, 3), strategy
+        assert key(log[0]) == best_key, strategy
+        assert key(action) == best_key, strategy
     assert len(EpisodeStore(tmp_path).list_episodes("paged_attention")) == 6
 
 
@@ -133,8 +137,35 @@ def test_leaderboard_and_replay_commands(tmp_path):
 
     _, _, _, _, ep = _run(tmp_path, "grid", 4)
     res = CliRunner().invoke(cli.main, ["leaderboard", "paged_attention", "--out", str(tmp_path)])
-    assert res.exit_code == 0 and "split=64 tile=0x0x0 stages=2" in res.output and ep in res.output, res.output
+    assert res.exit_code == 0 and "rows_per_cta=0 tile=296x0x0 flags=0 stages=0" in res.output and ep in res.output, \
+        res.output
     res = CliRunner().invoke(cli.main, ["replay", "paged_attention", ep, "--out", str(tmp_path)])
     assert res.exit_code == 0 and json.loads(res.output)["episode_id"] == ep
     res = CliRunner().invoke(cli.main, ["replay", "paged_attention", "nope", "--out", str(tmp_path)])
     assert res.exit_code != 0
+
+
+def test_leaderboard_gains_columns_added_after_it_was_written(tmp_path):
+    """A leaderboard written before the flags column existed is migrated in
+    place: old rows read back with flags NULL -> 0, new rows store it."""
+    import sqlite3
+
+    db = tmp_path / "lb.sqlite"
+    conn = sqlite3.connect(str(db))
+    conn.execute("CREATE TABLE leaderboard (id INTEGER PRIMARY KEY AUTOINCREMENT, op_name TEXT NOT NULL, "
+                 "shape TEXT NOT NULL, dtype TEXT NOT NULL, device TEXT NOT NULL, template_id TEXT, block_d INTEGER, "
+                 "num_warps INTEGER, num_stages INTEGER, vectorize INTEGER, threads INTEGER, rows_per_cta INTEGER, "
+                 "split INTEGER, tile_m INTEGER, tile_n INTEGER, tile_k INTEGER, latency_us_p50 REAL, speedup REAL, "
+                 "reward REAL, promoted INTEGER, achieved_GBps REAL, achieved_TOPS REAL, roofline_fraction REAL, "
+                 "num_gpus INTEGER, episode_id TEXT, timestamp REAL, "
+                 "UNIQUE(op_name, shape, dtype, device, template_id))")
+    conn.execute("INSERT INTO leaderboard (op_name, shape, dtype, device, template_id, block_d, num_warps, "
+                 "num_stages, vectorize, threads, rows_per_cta, split, tile_m, tile_n, tile_k, speedup) "
+                 "VALUES ('gemm', 'M=16', 'fp16', 'cuda', 'old', 128, 4, 3, 0, 0, 0, 0, 0, 0, 256, 1.0)")
+    conn.commit()
+    conn.close()
+    lb = LeaderboardStore(db)
+    assert lb.action_of(lb.best_config("gemm", "M=16", "fp16")).flags == 0
+    lb.upsert("gemm", "M=4096", "fp16", "cuda", OpAction("new", flags=2),
+              CandidateResult(compile_pass=True, verify_pass=True, speedup=2.0), "e1")
+    assert lb.action_of(lb.best_config("gemm", "M=4096", "fp16")).flags == 2

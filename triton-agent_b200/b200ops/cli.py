@@ -223,13 +223,34 @@ def warm_start_actions(state: OpState, templates: dict[str, Any], config_store, 
     return out
 
 
+def space_rows(op: str, parsed: dict[str, int], gen_fn=None) -> int:
+    """The row count b200_query_config_space selects an op's kernel by: GEMM
+    rows (B*M), new tokens of the paged append, sequences of the decode;
+    unspecified sizes take the input generator's defaults."""
+    import inspect
+
+    dflt = {}
+    if gen_fn is not None:
+        dflt = {k: p.default for k, p in inspect.signature(gen_fn).parameters.items()
+                if isinstance(p.default, int) and not isinstance(p.default, bool)}
+    get = lambda k, d=0: int(parsed.get(k, dflt.get(k, d)))  # noqa: E731
+    if op in ("quant_matmul", "matmul_epilogue"):
+        return get("B", 1) * get("M", 0)
+    if op == "rope_kv_append_paged":
+        return get("T", 0)
+    if op == "paged_attention":
+        return get("B", 0)
+    return 0
+
+
 def search(contract: OpContract, state: OpState, templates: dict[str, Any], eval_fn, strategy: str,
-           max_candidates: int, retry: int, store_path: Path, warm=()) -> tuple[list, list[CandidateResult]]:
+           max_candidates: int, retry: int, store_path: Path, warm=(), axes=None) -> tuple[list, list[CandidateResult]]:
     """Candidate search of `optimize` (reference cli.py:57-160): grid or
     best-of-n lists, or a bandit / policy-gradient / GRPO trainer choosing
     one candidate per step, with repair-and-retry of failed candidates.
-    `warm` candidates are evaluated first.  eval_fn(template_id, action)
-    returns the CandidateResult."""
+    `warm` candidates are evaluated first.  `axes` (OpAction field, values)
+    replaces the contract's search space when given.  eval_fn(template_id,
+    action) returns the CandidateResult."""
     from .agent.generator import generate_best_of_n, generate_grid
     from .agent.repairer import repair_action, should_retry
     from .microrl.trainer import Trainer
@@ -237,11 +258,12 @@ def search(contract: OpContract, state: OpState, templates: dict[str, Any], eval
     warm = list(warm)
     warm_keys = {a.arm_key() for _, a in warm}
     if strategy in ("grid", "best_of_n"):
-        gen = generate_grid(contract, state, templates) if strategy == "grid" else \
-            generate_best_of_n(contract, state, templates, n=max_candidates, seed=0)
+        gen = generate_grid(contract, state, templates, axes=axes) if strategy == "grid" else \
+            generate_best_of_n(contract, state, templates, n=max_candidates, seed=0, axes=axes)
         cands = (warm + [c for c in gen if c[1].arm_key() not in warm_keys])[:max_candidates]
         return cands, [eval_fn(t, a) for t, a in cands]
-    all_c = warm + [c for c in generate_grid(contract, state, templates) if c[1].arm_key() not in warm_keys]
+    all_c = warm + [c for c in generate_grid(contract, state, templates, axes=axes)
+                    if c[1].arm_key() not in warm_keys]
     trainer = Trainer(strategy=strategy, store_path=store_path)
     cands, results = [], []
     for step in range(max_candidates):
@@ -295,14 +317,23 @@ def record_outcome(state: OpState, cands: list, results: list[CandidateResult], 
 @click.option("--retry", default=1, type=int)
 @click.option("--out", default="episodes", help="directory for episodes, leaderboard.sqlite and best_configs.json")
 @click.option("--warm-start/--no-warm-start", default=True, help="evaluate the stored best configuration first")
+@click.option("--space", "space_mode", default="contract", type=click.Choice(["contract", "library"]),
+              help="contract: the contract's search space pruned to the parameters the selected kernel reads; "
+                   "library: every value b200_query_config_space lists")
 def optimize(op: str, shape: str, dtype: str, strategy: str, max_candidates: int, retry: int, out: str,
-             warm_start: bool) -> None:
-    """Searches the CUDA launch/tile space of OP and promotes the best variant."""
+             warm_start: bool, space_mode: str) -> None:
+    """Searches the CUDA launch/tile space of OP and promotes the best variant.
+
+    The kernel's all-default launch (after any stored best) is always among
+    the candidates, and the episode records it, so a promoted configuration
+    is measured against the default on the same inputs."""
+    from .agent.generator import _axes, default_action, library_axes
     from .agent.promoter import should_promote
     from .agent.selector import select_best
     from .core.profiler import time_device
     from .core.storage import LeaderboardStore
     from .microrl.trainer import ShapeConfigStore
+    from .runtime import lib as L
 
     ensure_registered(op)
     contract = get_registry().get(op)
@@ -319,17 +350,30 @@ def optimize(op: str, shape: str, dtype: str, strategy: str, max_candidates: int
     state.baseline_latency_us = baseline_us
 
     outdir = Path(out)
+    space = L.config_space(op, space_rows(op, parsed, gen_fn))
+    axes = library_axes(space) if (space_mode == "library" and space) else _axes(contract, space)
     warm = warm_start_actions(state, templates, ShapeConfigStore(outdir / "best_configs.json"),
                               LeaderboardStore(outdir / "leaderboard.sqlite")) if warm_start else []
+    stored = [a.to_dict() for _, a in warm]
+    keys = {a.arm_key() for _, a in warm}
+    defaults = [(t, default_action(t, axes)) for t in sorted(templates)]
+    warm += [(t, a) for t, a in defaults if a.arm_key() not in keys]
     cands, results = search(contract, state, templates,
                             lambda t, a: evaluate(op, contract, templates[t], a, state, inputs, ref_out, baseline_us),
-                            strategy, max_candidates, retry, outdir / "best_configs.json", warm)
+                            strategy, max_candidates, retry, outdir / "best_configs.json", warm, axes=axes)
     best_i, best = select_best(cands, results)
     best.promoted = should_promote(best, contract)
+    dkeys = {a.arm_key(): t for t, a in defaults}
+    default_res = [{"template": t, "action": a.to_dict(), "result": r.to_dict()}
+                   for (t, a), r in zip(cands, results) if a.arm_key() in dkeys]
     path, _ = record_outcome(state, cands, results, best_i, outdir,
                              {"strategy": strategy, "shape": parsed, "baseline_latency_us": baseline_us,
-                              "warm_start": [a.to_dict() for _, a in warm]})
-    click.echo(f"best {cands[best_i][0]} {cands[best_i][1].launch_cfg()} p50={best.latency_us_p50:.1f}us "
+                              "warm_start": stored, "config_space": space, "space_mode": space_mode,
+                              "axes": {a: v for a, v in axes}, "default": default_res})
+    vs = ""
+    if default_res and default_res[0]["result"]["latency_us_p50"] > 0:
+        vs = f" default_p50={default_res[0]['result']['latency_us_p50']:.1f}us"
+    click.echo(f"best {cands[best_i][0]} {cands[best_i][1].launch_cfg()} p50={best.latency_us_p50:.1f}us{vs} "
                f"speedup={best.speedup:.2f}x reward={best.reward:.2f} promoted={best.promoted} -> {path}")
 
 
@@ -350,7 +394,8 @@ def leaderboard(op: str, shape: str, dtype: str, out: str, limit: int) -> None:
         return
     for r in rows:
         click.echo(f"{r['shape']} {r['dtype']} {r['template_id']} threads={r['threads']} split={r['split']} "
-                   f"tile={r['tile_m']}x{r['tile_n']}x{r['tile_k']} stages={r['num_stages']} "
+                   f"rows_per_cta={r['rows_per_cta']} tile={r['tile_m']}x{r['tile_n']}x{r['tile_k']} "
+                   f"flags={r.get('flags') or 0} stages={r['num_stages']} "
                    f"p50={r['latency_us_p50']:.1f}us speedup={r['speedup']:.2f}x "
                    f"roofline={r['roofline_fraction']:.2f} promoted={bool(r['promoted'])} ep={r['episode_id']}")
 

@@ -2,7 +2,7 @@
 
 Field names and to_dict/from_dict round trips are those of the reference.
 OpAction gains the CUDA launch/tile parameters of b200_launch_cfg (threads,
-rows_per_cta, split, tile_m, tile_n, tile_k) with 0 = kernel default, and
+rows_per_cta, split, tile_m, tile_n, tile_k, flags) with 0 = kernel default, and
 CandidateResult gains roofline fields; both default so old records load.
 """
 
@@ -38,7 +38,7 @@ class OpState:
                    historical_best_config=data.get("historical_best_config"), shape=data.get("shape", ""))
 
 
-CUDA_FIELDS = ("threads", "rows_per_cta", "split", "tile_m", "tile_n", "tile_k")
+CUDA_FIELDS = ("threads", "rows_per_cta", "split", "tile_m", "tile_n", "tile_k", "flags")
 
 
 @dataclass
@@ -55,6 +55,7 @@ class OpAction:
     tile_m: int = 0
     tile_n: int = 0
     tile_k: int = 0
+    flags: int = 0  # kernel-variant bits of the op (b200_launch_cfg.flags)
 
     def to_dict(self) -> dict[str, Any]:
         return asdict(self)

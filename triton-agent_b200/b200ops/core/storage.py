@@ -4,7 +4,7 @@ EpisodeStore writes one JSON record per evaluated candidate under
 <dir>/<op>/<episode_id>/record.json (storage.py:12-65).  LeaderboardStore keeps
 the best configuration per (op, shape, dtype, device, template) in SQLite
 (storage.py:68-165) with the CUDA launch parameters this backend tunes
-(threads, rows_per_cta, split, tile_m/n/k, stages) and the roofline fields of
+(threads, rows_per_cta, split, tile_m/n/k, flags, stages) and the roofline fields of
 the measurement (achieved GB/s or TOPS, roofline fraction) instead of the
 reference's Triton block/warp columns only.  Together with
 microrl.trainer.ShapeConfigStore they let a later tuning run start from the
@@ -53,7 +53,7 @@ _COLUMNS = (
     ("device", "TEXT NOT NULL"), ("template_id", "TEXT"),
     ("block_d", "INTEGER"), ("num_warps", "INTEGER"), ("num_stages", "INTEGER"), ("vectorize", "INTEGER"),
     ("threads", "INTEGER"), ("rows_per_cta", "INTEGER"), ("split", "INTEGER"), ("tile_m", "INTEGER"),
-    ("tile_n", "INTEGER"), ("tile_k", "INTEGER"),
+    ("tile_n", "INTEGER"), ("tile_k", "INTEGER"), ("flags", "INTEGER"),
     ("latency_us_p50", "REAL"), ("speedup", "REAL"), ("reward", "REAL"), ("promoted", "INTEGER"),
     ("achieved_GBps", "REAL"), ("achieved_TOPS", "REAL"), ("roofline_fraction", "REAL"), ("num_gpus", "INTEGER"),
     ("episode_id", "TEXT"), ("timestamp", "REAL"),
@@ -69,6 +69,11 @@ class LeaderboardStore:
         with self._conn() as conn:
             conn.execute(f"CREATE TABLE IF NOT EXISTS leaderboard (id INTEGER PRIMARY KEY AUTOINCREMENT, {cols}, "
                          f"UNIQUE({', '.join(_KEY)}))")
+            # a table written before a column existed gains it (NULL in old rows)
+            have = {r[1] for r in conn.execute("PRAGMA table_info(leaderboard)")}
+            for n, t in _COLUMNS:
+                if n not in have:
+                    conn.execute(f"ALTER TABLE leaderboard ADD COLUMN {n} {t.replace(' NOT NULL', '')}")
 
     @contextmanager
     def _conn(self) -> Iterator[sqlite3.Connection]:
@@ -89,7 +94,7 @@ class LeaderboardStore:
                "template_id": action.template_id, "block_d": action.block_d, "num_warps": action.num_warps,
                "num_stages": action.num_stages, "vectorize": int(bool(action.vectorize)),
                "threads": action.threads, "rows_per_cta": action.rows_per_cta, "split": action.split,
-               "tile_m": action.tile_m, "tile_n": action.tile_n, "tile_k": action.tile_k,
+               "tile_m": action.tile_m, "tile_n": action.tile_n, "tile_k": action.tile_k, "flags": action.flags,
                "latency_us_p50": result.latency_us_p50, "speedup": result.speedup, "reward": result.reward,
                "promoted": int(bool(result.promoted)), "achieved_GBps": result.achieved_GBps,
                "achieved_TOPS": result.achieved_TOPS, "roofline_fraction": result.roofline_fraction,
@@ -125,4 +130,4 @@ class LeaderboardStore:
         return OpAction(template_id=row["template_id"], block_d=row["block_d"], num_warps=row["num_warps"],
                         num_stages=row["num_stages"], vectorize=bool(row["vectorize"]), threads=row["threads"],
                         rows_per_cta=row["rows_per_cta"], split=row["split"], tile_m=row["tile_m"],
-                        tile_n=row["tile_n"], tile_k=row["tile_k"])
+                        tile_n=row["tile_n"], tile_k=row["tile_k"], flags=row.get("flags") or 0)

@@ -79,6 +79,7 @@ SIGNATURES = {
     "b200_kernel_list": (c_char_p, []),
     "b200_last_error_detail": (c_char_p, []),
     "b200_read_device_error": (c_int, [POINTER(c_int32), P]),
+    "b200_query_config_space": (c_char_p, [c_char_p, I64_]),
     "b200_set_peer_wait_timeout_us": (c_int, [I64_]),
     "b200_rmsnorm": (c_int, [P, P, P, I64_, I64_, c_float, c_int32, c_int32, PCFG, P]),
     "b200_rmsnorm_quant_int8": (c_int, [P, P, P, P, P, I64_, I64_, c_float, c_int32, c_int32, PCFG, P]),
@@ -166,6 +167,16 @@ def check(status: int, op: str) -> None:
 
 def kernel_names() -> list[str]:
     return [k for k in load().b200_kernel_list().decode().split("\n") if k]
+
+
+def config_space(op: str, rows: int = 0) -> dict | None:
+    """The launch parameters the kernel selected for `op` at `rows` rows
+    reads, with their legal values (b200_query_config_space), or None for an
+    op the library does not know."""
+    import json
+
+    txt = load().b200_query_config_space(op.encode(), int(rows))
+    return json.loads(txt.decode()) if txt else None
 
 
 def version() -> int:

@@ -6,6 +6,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -144,6 +145,8 @@ const char* b200_kernel_list(void) {
          "kv_scatter_kernel\n"
          "rope_kv_append_paged_kernel\n"
          "rope_kv_append_paged_fast_kernel\n"
+         "rope_kv_append_paged_rows_kernel\n"
+         "slot_owner_kernel\n"
          "paged_decode_flat_kernel\n"
          "paged_decode_kernel\n"
          "paged_decode_generic_kernel\n"
@@ -220,6 +223,93 @@ int b200_ipc_close(void* dev_ptr, int64_t offset) {
     return B200_ERR_LAUNCH;
   }
   return B200_OK;
+}
+
+// Launch parameters the tuner may search, per op: the kernel the op's
+// default dispatch selects for `rows` rows (GEMM: M; decode: sequences;
+// 0: the op's benchmark shape), and for each b200_launch_cfg field that
+// kernel reads, the values it accepts (0 = the kernel's default).  Fields not
+// listed are ignored by that kernel.  The text is JSON, valid until the next
+// call on the same thread.
+const char* b200_query_config_space(const char* op, int64_t rows) {
+  static thread_local std::string out;
+  if (op == nullptr) return nullptr;
+  const int sms = b200::device_sm_count();
+  const std::string o(op);
+  std::string kernel, fields;
+  auto field = [&](const char* name, std::initializer_list<int64_t> vals, const char* meaning) {
+    if (!fields.empty()) fields += ",";
+    fields += "\"";
+    fields += name;
+    fields += "\":{\"values\":[";
+    bool first = true;
+    for (int64_t v : vals) {
+      if (!first) fields += ",";
+      fields += std::to_string(v);
+      first = false;
+    }
+    fields += "],\"meaning\":\"";
+    fields += meaning;
+    fields += "\"}";
+  };
+  if (o == "rmsnorm") {
+    kernel = "rmsnorm_row_kernel";
+    field("threads", {0, 128, 256, 512, 1024}, "CTA size (0: 256, or fewer for short rows)");
+  } else if (o == "rmsnorm_quant") {
+    kernel = "rmsnorm_quant_row_kernel";
+    field("threads", {0, 64, 128, 256, 512, 1024}, "CTA size (0: about four 16-byte vectors per thread)");
+    field("rows_per_cta", {0, 1, 2, 4}, "rows per CTA (0: 1; more than 1 only with <= 256 threads)");
+  } else if (o == "rope") {
+    kernel = "rope_kernel";
+    field("threads", {0, 64, 128, 256}, "CTA size, at most 256 (0: 256)");
+  } else if (o == "kv_append" || o == "paged_kv" || o == "rope_kv_append") {
+    kernel = "kv_scatter_kernel";
+    field("threads", {0, 128, 256, 512, 1024}, "CTA size (0: all rows' lanes, up to 1024)");
+  } else if (o == "rope_kv_append_paged") {
+    if (rows > 512) {
+      kernel = "rope_kv_append_paged_rows_kernel";
+      field("rows_per_cta", {0, 2, 3, 4, 6, 8, 12}, "rows of a token per thread (0: 4)");
+    } else {
+      kernel = "rope_kv_append_paged_fast_kernel";
+      field("threads", {0, 128, 256, 512},
+            "0: the single-pass kernel (one CTA per token); > 0: the general kernel with this CTA size");
+    }
+  } else if (o == "paged_attention") {
+    kernel = "paged_decode_flat_kernel";
+    field("rows_per_cta", {0, 1, 2, 4, 8}, "kv heads per CTA, a divisor of H_kv (0: the largest <= 8 that fits)");
+    field("stages", {0, 2, 3, 4}, "KV page ring depth (0: about 128 KB of pages in flight)");
+    field("tile_m", {0, 2 * (int64_t)sms}, "CTAs of the persistent grid (0: one per SM)");
+    field("tile_k", {0, 10, 25, 50}, "percent of the block-table entries handed out as claimed chunks (0: none)");
+    field("tile_n", {0, 1, 2, 8}, "pages per claimed chunk (0: 4)");
+  } else if (o == "quant_matmul") {
+    if (rows > 0 && rows <= 64) {
+      kernel = "int8_gemm_stream_kernel";
+      field("tile_k", {0, 128, 256, 512, 1024}, "bytes of K per ring stage (0: 512, 256 for M > 32)");
+      field("stages", {0, 4, 6, 8, 10, 12, 14, 16}, "ring depth (0: 16, or as many as fit)");
+    } else if (rows > 0 && rows <= 128) {
+      kernel = "int8_gemm_tcgen05_kernel";
+      field("tile_n", {0, 128, 256}, "output columns per tile (0: 256)");
+      field("stages", {0, 2, 3, 4, 5, 6, 7, 8}, "ring depth (0: 8)");
+    } else {
+      kernel = "int8_gemm_pair_kernel";
+      field("stages", {0, 2, 3, 4, 5, 6, 7, 8}, "ring depth (0: 8)");
+      field("flags", {0, 2}, "2: one-SM persistent kernel (128 x tile_n tiles) instead of CTA pairs");
+      field("tile_n", {0, 128, 256}, "output columns per tile of the one-SM kernel (0: 256)");
+    }
+  } else if (o == "matmul_epilogue") {
+    kernel = "int8_gemm_pair_kernel (kind::f16)";
+    field("stages", {0, 2, 3, 4, 5, 6, 7, 8}, "ring depth (0: 8)");
+  } else if (o == "flash_attn_like") {
+    kernel = "flash_fwd3_tcgen05_kernel";
+    field("split", {0, 1, 2, 4, 8, 16}, "heads per scheduling group sharing K/V in L2 (0: 8)");
+    field("tile_k", {0, 1, 2, 3, 4}, "exponential pairs of every 8 on the FMA pipe (0: 2; 4: none)");
+    field("flags", {0, 16}, "16: persistent kernel (one CTA per SM taking work items)");
+  } else {
+    return nullptr;
+  }
+  out = "{\"op\":\"" + o + "\",\"rows\":" + std::to_string(rows) + ",\"kernel\":\"" + kernel +
+        "\",\"sm_count\":" + std::to_string(sms) + ",\"fields\":{" + fields + "}}";
+  return out.c_str();
 }
 
 int b200_set_peer_wait_timeout_us(int64_t us) {
