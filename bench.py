@@ -1,6 +1,7 @@
 """Benchmark of the paged-decode hot path on B200 (one JSON line on rank 0).
 
-A step is one decode step of 64 sequences on one GPU:
+A step is one decode step of 64 sequences per GPU (a global batch of 64 x N
+sequences sharded by KV bytes, each rank owning its share's pages):
   1. fused RoPE(q, k) + paged K/V append of the step's 64 new tokens
      (32 q / 8 kv heads, head dim 128, bf16, 65536 x 16-token cache blocks),
   2. paged-attention decode over context lengths ~ U[512, 8192]
@@ -328,10 +329,17 @@ def run_b200(args, ws, rank, local, dist):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     L.load()
+    from b200ops.dist.sharding import imbalance, shard_sequences
+
     seed = 1000 * rank
+    # a global batch of 64 sequences per GPU, sharded by KV bytes (longest
+    # first onto the least-loaded rank): each rank owns its share's KV pages
+    ctx_all = WL.context_lengths(N_SEQ * ws)
+    parts = shard_sequences(ctx_all.tolist(), ws)
+    mine = ctx_all[parts[rank]]
     cache = WL.paged_cache(num_blocks=NBLK, block_size=BS, Hkv=HKV, D=D, device=dev, seed=seed)
-    app = WL.decode_append_inputs(cache, n_tok=N_SEQ, Hq=HQ, device=dev, seed=seed)
-    att = WL.decode_attention_inputs(cache, B=N_SEQ, Hq=HQ, device=dev, seed=seed)
+    app = WL.decode_append_inputs(cache, n_tok=len(mine), Hq=HQ, device=dev, seed=seed)
+    att = WL.decode_attention_inputs(cache, Hq=HQ, device=dev, seed=seed, context_len=mine)
     q_out = torch.empty_like(app["q"])
     out = torch.empty_like(att["q"])
     stream = torch.cuda.current_stream(dev)
@@ -508,9 +516,14 @@ def run_b200(args, ws, rank, local, dist):
         "decode_step_append": {
             "what": "the step's fused RoPE + paged append of 64 new tokens alone (n appends in one graph)",
             "us": append_ms * 1e3, "tokens_per_s": N_SEQ * ws / (append_ms / 1e3),
-            "GBps": WL.append_bytes(N_SEQ, HQ, HKV, D) / append_ms / 1e6,
-            "frac": WL.append_bytes(N_SEQ, HQ, HKV, D) / append_ms / 1e6 / peaks["hbm_gbs"],
-            "algorithmic_bytes": WL.append_bytes(N_SEQ, HQ, HKV, D), "bound": "launch/latency (1.6 MB per call)"},
+            "GBps": WL.append_bytes(len(mine), HQ, HKV, D) / append_ms / 1e6,
+            "frac": WL.append_bytes(len(mine), HQ, HKV, D) / append_ms / 1e6 / peaks["hbm_gbs"],
+            "algorithmic_bytes": WL.append_bytes(len(mine), HQ, HKV, D),
+            "bound": "launch/latency (1.6 MB per call)"},
+        "sharding": {"global_sequences": N_SEQ * ws, "sequences_per_rank": [len(p) for p in parts],
+                     "kv_tokens_per_rank": [int(ctx_all[p].sum()) for p in parts],
+                     "imbalance": imbalance(ctx_all.tolist(), parts),
+                     "rule": "longest first onto the least-loaded rank (b200ops.dist.sharding.shard_sequences)"},
         **({"per_rank": per_rank} if ws > 1 else {}),
         "gpu_launches": 2 * n,
         "clocks": clocks,

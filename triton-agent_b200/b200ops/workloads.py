@@ -83,15 +83,28 @@ def decode_append_inputs(cache: PagedCache, n_tok=64, Hq=32, max_pos=4096, theta
     return dict(q=q, k=k, v=v, positions=positions, cos=cos, sin=sin, slot_mapping=slots)
 
 
+def context_lengths(n_seq: int, ctx_lo=512, ctx_hi=8192, seed=0) -> torch.Tensor:
+    """Context lengths ~ U{ctx_lo..ctx_hi} of a global batch of sequences
+    (host int64), drawn once so that every rank shards the same batch."""
+    g = torch.Generator().manual_seed(seed + 6000)
+    return torch.randint(ctx_lo, ctx_hi + 1, (n_seq,), generator=g, dtype=torch.int64)
+
+
 def decode_attention_inputs(cache: PagedCache, B=64, Hq=32, ctx_lo=512, ctx_hi=8192, device="cuda", seed=0,
-                            index_dtype=torch.int32):
-    """Inputs of one paged-attention decode step over `cache`."""
+                            index_dtype=torch.int32, context_len: torch.Tensor | None = None):
+    """Inputs of one paged-attention decode step over `cache`.  With
+    `context_len` (this rank's share of a global batch) B is its length and
+    the lengths are used as given."""
     Hkv, D = cache.k_cache.shape[2:]
     bs = cache.block_size
     g = _gen(device, seed + 3000)
     dt = cache.k_cache.dtype
+    if context_len is not None:
+        B = int(context_len.numel())
     q = torch.randn(B, Hq, D, generator=g, device=device, dtype=torch.float32).to(dt)
     ctx = torch.randint(ctx_lo, ctx_hi + 1, (B,), generator=g, device=device, dtype=torch.int64)
+    if context_len is not None:
+        ctx = context_len.to(device=device, dtype=torch.int64)
     max_blocks = (ctx_hi + bs - 1) // bs
     if B * max_blocks > cache.num_blocks:
         raise ValueError("cache too small for disjoint block tables")
