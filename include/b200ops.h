@@ -121,7 +121,9 @@ int b200_rmsnorm(const void* x, const void* weight, void* y, int64_t rows,
  * == 0 and 16-byte aligned x/weight/y (B200_ERR_ALIGNMENT otherwise).
  * cfg: threads (CTA size, multiple of 32, default about D / 32 for 16-bit
  * dtypes), rows_per_cta (1, 2 or 4 rows per CTA; more than one only with at
- * most 256 threads; default 1). */
+ * most 256 threads; default 1); flags bit 0: one CTA per row even where the
+ * persistent row loop applies (16-bit rows of four 16-byte vectors per
+ * thread, at most 256 threads). */
 int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t* q, float* scale,
                             void* y, int64_t rows, int64_t D, float eps, int32_t dtype,
                             int32_t weight_dtype, const b200_launch_cfg* cfg, void* stream);

@@ -31,9 +31,11 @@ def inputs(rows, D, dtype, wdtype, dev, seed=0):
     (64, 4096, torch.float16, torch.float16), (9, 1000, torch.float32, torch.float32),
     (8 * 2048, 4096, torch.bfloat16, torch.bfloat16), (5, 64, torch.float16, torch.float32),
 ])
-# default CTA size / b200_rmsnorm's CTA size for D=4096, with 1, 2 and 4 rows per CTA
-@pytest.mark.parametrize("cfg", [None, {"threads": 256}, {"threads": 256, "rows_per_cta": 1},
-                                 {"rows_per_cta": 4}, {"threads": 128, "rows_per_cta": 2}])
+# default (persistent kernel for 16-bit rows of four vectors per thread) /
+# one CTA per row (flags 1) / b200_rmsnorm's CTA size for D=4096, with 1, 2
+# and 4 rows per CTA
+@pytest.mark.parametrize("cfg", [None, {"flags": 1}, {"threads": 256}, {"threads": 256, "rows_per_cta": 1},
+                                 {"rows_per_cta": 4}, {"threads": 128, "rows_per_cta": 2}, {"threads": 64}])
 def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
     x, w = inputs(rows, D, dtype, wdtype, cuda_device)
     q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg=cfg)
@@ -59,6 +61,29 @@ def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
         torch.testing.assert_close(y.float(), y_ref.float(), rtol=tol, atol=tol)
     q2, s2 = K.rmsnorm_quant_int8(x, w, 1e-6, cfg=cfg)  # without y
     assert torch.equal(q2, q) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("rows,D", [(1, 4096), (7, 8192), (300, 1024), (2048, 4104)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_persistent_kernel_row_loop_and_tails(rows, D, dtype, cuda_device):
+    """The persistent kernel's row loop (fewer CTAs than rows, the next row
+    prefetched), partial last vectors (D not a multiple of the CTA's
+    vectors), widths whose codes land on +-127 and rows that are all zero:
+    codes exactly the oracle quantiser's on the kernel's y, and equal to the
+    one-CTA-per-row kernel's."""
+    x, w = inputs(rows, D, dtype, dtype, cuda_device, seed=rows)
+    x[0, :] = 0
+    if rows > 3:
+        x[3, :] = x[3, :].abs()  # one-signed row: the maximum lands exactly on 127
+    q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True)
+    q1, s1, y1 = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg={"flags": 1})
+    torch.cuda.synchronize()
+    q_o, s_o = O.quantize_int8(y.cpu())
+    assert torch.equal(q.cpu(), q_o) and torch.equal(s.cpu(), s_o.reshape(-1).float())
+    torch.testing.assert_close(y.float(), y1.float(), rtol=1e-2, atol=1e-2)
+    if torch.equal(y, y1):
+        assert torch.equal(q, q1) and torch.equal(s, s1)
+    assert int(q.abs().max()) <= 127 and int(q[0].abs().max()) == 0
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])

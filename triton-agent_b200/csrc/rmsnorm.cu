@@ -248,6 +248,140 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
   }
 }
 
+// Persistent variant for 16-bit rows of NV = 4 vectors per thread (the
+// default CTA size for D >= 1024): a grid of the resident CTA count loops
+// over rows, so the weights are widened to fp32 once per CTA and kept in
+// registers, and the next row's x is loaded while the current row is reduced
+// and quantised.  Per element it does the same arithmetic as
+// rmsnorm_quant_row_kernel with less around it:
+//  - max|y| is taken on the fp32 products before their rounding to T (the
+//    rounding is monotonic, so the rounded maximum is the maximum of the
+//    rounded values) instead of re-widening the rounded row;
+//  - bf16: q = RN_bf16(y * RN(1/s)) without Markstein's correction.  y and s
+//    have 8-bit significands, so y / s is either exactly representable in
+//    bf16 or a fraction p/q (q odd, q <= 255) at least 2^-17 (relative) away
+//    from every bf16 rounding midpoint; y * RN(1/s) is within 2^-23 of y / s,
+//    so both round to the same bf16 value (and the fp32 rounding of the
+//    quotient, which the reference performs first, cannot land on a
+//    midpoint either).  fp16's 11-bit significands leave no such margin, so
+//    fp16 keeps the corrected quotient;
+//  - the clamp to [-127, 127] is one min.xorsign.abs on the packed pair
+//    (rint commutes with clamping at an integer), before the integer
+//    rounding by adding 1.5 * 2^23.
+// The sum of squares is accumulated in the same order as
+// rmsnorm_quant_row_kernel's with one row per CTA of the same size.
+template <typename T, typename W, bool FULL>
+__global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
+    const T* __restrict__ x, const W* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ scale,
+    T* __restrict__ y, int64_t rows, int D, float eps) {
+  constexpr int VN = Vec<T>::N;  // 8
+  constexpr int NV = 4;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  __shared__ float red[32], red2[32];
+  const int nvec = D / VN;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  auto live = [&](int i) { return FULL || tid + i * nt < nvec; };
+  float wf[NV][VN];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (live(i)) {
+      load_weights<W, VN>(w + (int64_t)(tid + i * nt) * VN, wf[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VN; ++j) wf[i][j] = 0.f;
+    }
+  }
+  uint4 cur[NV];
+  int64_t r = blockIdx.x;
+  if (r < rows) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      if (live(i)) cur[i] = ldg_stream16(x + r * D + (int64_t)(tid + i * nt) * VN);
+  }
+  for (; r < rows; r += gridDim.x) {
+    // the next row's loads are in flight during this row's two reductions
+    uint4 nxt[NV];
+    const int64_t rn = r + gridDim.x;
+    if (rn < rows) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (live(i)) nxt[i] = ldg_stream16(x + rn * D + (int64_t)(tid + i * nt) * VN);
+    }
+    float f[NV][VN];
+    float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (live(i)) {
+        unpack16<T>(cur[i], f[i]);
+#pragma unroll
+        for (int j = 0; j < VN; j += 2)
+          sm100::ffma2(ss0, ss1, f[i][j], f[i][j + 1], f[i][j], f[i][j + 1], ss0, ss1);
+      }
+    }
+    const float ss = block_sum(ss0 + ss1, red);
+    const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (live(i)) {
+#pragma unroll
+        for (int j = 0; j < VN; j += 2) {
+          sm100::fmul2_bcast(f[i][j], f[i][j + 1], f[i][j], f[i][j + 1], rstd);
+          sm100::fmul2(f[i][j], f[i][j + 1], f[i][j], f[i][j + 1], wf[i][j], wf[i][j + 1]);
+          amax = sm100::fmax3(amax, fabsf(f[i][j]), fabsf(f[i][j + 1]));
+        }
+        cur[i] = pack16<T>(f[i]);  // y rounded to T
+        if (y != nullptr) stg_stream16(y + r * D + (int64_t)(tid + i * nt) * VN, cur[i]);
+      }
+    }
+    amax = block_max(amax, red2);
+    const float s = finish_scale<T>(round_to<T>(amax));
+    const float rs = __frcp_rn(s);
+    if (tid == 0) scale[r] = s;
+    int8_t* qr = q + r * D;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (!live(i)) continue;
+      const uint32_t* yw = reinterpret_cast<const uint32_t*>(&cur[i]);
+      uint32_t h[VN / 2];
+#pragma unroll
+      for (int k = 0; k < VN / 2; ++k) {
+        float v0, v1;
+        if constexpr (kBF16) {
+          const float y0 = __uint_as_float(yw[k] << 16), y1 = __uint_as_float(yw[k] & 0xFFFF0000u);
+          float q0, q1;
+          sm100::fmul2_bcast(q0, q1, y0, y1, rs);
+          uint32_t pk;
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(q1), "f"(q0));
+          asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x42FE42FEu));  // +-127
+          v0 = __uint_as_float(pk << 16);
+          v1 = __uint_as_float(pk & 0xFFFF0000u);
+        } else {
+          const float2 yf = __half22float2(*reinterpret_cast<const __half2*>(&yw[k]));
+          float q0, q1, e0, e1;
+          sm100::fmul2_bcast(q0, q1, yf.x, yf.y, rs);
+          sm100::ffma2(e0, e1, q0, q1, -s, -s, yf.x, yf.y);
+          sm100::ffma2(v0, v1, e0, e1, rs, rs, q0, q1);
+          uint32_t pk;
+          asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(v1), "f"(v0));
+          asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x57F057F0u));  // +-127
+          const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(&pk));
+          v0 = vf.x;
+          v1 = vf.y;
+        }
+        sm100::ffma2_bcast(v0, v1, v0, v1, 1.0f, 12582912.0f);  // low byte = rint as int8
+        h[k] = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x0040);
+      }
+      uint2 pk2;
+      pk2.x = __byte_perm(h[0], h[1], 0x5410);
+      pk2.y = __byte_perm(h[2], h[3], 0x5410);
+      *reinterpret_cast<uint2*>(qr + (int64_t)(tid + i * nt) * VN) = pk2;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+  }
+}
+
 // General path for any D and any alignment: two passes over the row, the
 // second one served mostly from L1/L2.
 template <typename T, typename W>
@@ -378,6 +512,23 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     int R = (cfg && cfg->rows_per_cta > 0) ? cfg->rows_per_cta : kQuantRowsPerCta;
     if (R != 1 && R != 2 && R != 4) return B200_ERR_BAD_ARG;
     if (nv > 4 || threads > 256) R = 1;  // multi-row CTAs are compiled for <= 256 threads
+    // 16-bit rows of four vectors per thread: the persistent kernel (flags
+    // bit 0: one CTA per row instead), one CTA per resident slot
+    if constexpr (!std::is_same<T, float>::value) {
+      if (nv == 4 && threads <= 256 && R == 1 && !(cfg && (cfg->flags & 1))) {
+        const bool full = nvec % threads == 0 && nvec / threads == 4;
+        auto kern = full ? rmsnorm_quant_persistent_kernel<T, W, true> : rmsnorm_quant_persistent_kernel<T, W, false>;
+        int per_sm = 0;
+        if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0);
+            e != cudaSuccess)
+          return launch_status(e);
+        if (per_sm < 1) per_sm = 1;
+        const int64_t slots = (int64_t)per_sm * device_sm_count();
+        const unsigned grid = (unsigned)(rows < slots ? rows : slots);
+        kern<<<grid, threads, 0, s>>>(xp, wp, q, scale, yp, rows, (int)D, eps);
+        return launch_status(cudaGetLastError());
+      }
+    }
     auto go = [&](auto nv_tag, auto r_tag) -> int {
       constexpr int NV = decltype(nv_tag)::value, RR = decltype(r_tag)::value;
       const dim3 grid((unsigned)((rows + RR - 1) / RR));

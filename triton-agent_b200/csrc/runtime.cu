@@ -259,6 +259,7 @@ const char* b200_query_config_space(const char* op, int64_t rows) {
     kernel = "rmsnorm_quant_row_kernel";
     field("threads", {0, 64, 128, 256, 512, 1024}, "CTA size (0: about four 16-byte vectors per thread)");
     field("rows_per_cta", {0, 1, 2, 4}, "rows per CTA (0: 1; more than 1 only with <= 256 threads)");
+    field("flags", {0, 1}, "1: one CTA per row instead of the persistent row loop (16-bit rows)");
   } else if (o == "rope") {
     kernel = "rope_kernel";
     field("threads", {0, 64, 128, 256}, "CTA size, at most 256 (0: 256)");
