@@ -248,8 +248,7 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
   }
 }
 
-// Persistent variant for 16-bit rows of NV = 4 vectors per thread (the
-// default CTA size for D >= 1024): a grid of the resident CTA count loops
+// Persistent variant for 16-bit rows of NV = 2 or 4 vectors per thread: a grid of the resident CTA count loops
 // over rows, so the weights are widened to fp32 once per CTA and kept in
 // registers, and the next row's x is loaded while the current row is reduced
 // and quantised.  Per element it does the same arithmetic as
@@ -270,16 +269,16 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
 //    rounding by adding 1.5 * 2^23.
 // The sum of squares is accumulated in the same order as
 // rmsnorm_quant_row_kernel's with one row per CTA of the same size.
-template <typename T, typename W, bool FULL>
+template <typename T, typename W, bool FULL, int NV>
 __global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
     const T* __restrict__ x, const W* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ scale,
     T* __restrict__ y, int64_t rows, int D, float eps) {
   constexpr int VN = Vec<T>::N;  // 8
-  constexpr int NV = 4;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   __shared__ float red[32], red2[32];
   const int nvec = D / VN;
   const int tid = threadIdx.x, nt = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = (nt + 31) >> 5;
   auto live = [&](int i) { return FULL || tid + i * nt < nvec; };
   float wf[NV][VN];
 #pragma unroll
@@ -318,7 +317,14 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
           sm100::ffma2(ss0, ss1, f[i][j], f[i][j + 1], f[i][j], f[i][j + 1], ss0, ss1);
       }
     }
-    const float ss = block_sum(ss0 + ss1, red);
+    // block reductions: a shuffle sum (redux.sync for the max) per warp, then
+    // every thread combines the per-warp values from shared memory in warp
+    // order (no second shuffle chain)
+    float ss = warp_sum(ss0 + ss1);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    ss = red[0];
+    for (int k = 1; k < nwarps; ++k) ss += red[k];
     const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
     float amax = 0.f;
 #pragma unroll
@@ -334,7 +340,11 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
         if (y != nullptr) stg_stream16(y + r * D + (int64_t)(tid + i * nt) * VN, cur[i]);
       }
     }
-    amax = block_max(amax, red2);
+    asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(amax) : "f"(amax));
+    if (lane == 0) red2[warp] = amax;
+    __syncthreads();
+    amax = red2[0];
+    for (int k = 1; k < nwarps; ++k) amax = fmaxf(amax, red2[k]);
     const float s = finish_scale<T>(round_to<T>(amax));
     const float rs = __frcp_rn(s);
     if (tid == 0) scale[r] = s;
@@ -354,8 +364,10 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
           uint32_t pk;
           asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(q1), "f"(q0));
           asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x42FE42FEu));  // +-127
-          v0 = __uint_as_float(pk << 16);
-          v1 = __uint_as_float(pk & 0xFFFF0000u);
+          // widen each half and add 1.5 * 2^23 in one mixed-precision add:
+          // the low byte of the sum's bits is rint(v) as int8
+          asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.bf16 %0, l, %3; add.rn.f32.bf16 %1, h, %3; }"
+              : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
         } else {
           const float2 yf = __half22float2(*reinterpret_cast<const __half2*>(&yw[k]));
           float q0, q1, e0, e1;
@@ -365,11 +377,9 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
           uint32_t pk;
           asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(v1), "f"(v0));
           asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x57F057F0u));  // +-127
-          const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(&pk));
-          v0 = vf.x;
-          v1 = vf.y;
+          asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.f16 %0, l, %3; add.rn.f32.f16 %1, h, %3; }"
+              : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
         }
-        sm100::ffma2_bcast(v0, v1, v0, v1, 1.0f, 12582912.0f);  // low byte = rint as int8
         h[k] = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x0040);
       }
       uint2 pk2;
@@ -512,12 +522,15 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     int R = (cfg && cfg->rows_per_cta > 0) ? cfg->rows_per_cta : kQuantRowsPerCta;
     if (R != 1 && R != 2 && R != 4) return B200_ERR_BAD_ARG;
     if (nv > 4 || threads > 256) R = 1;  // multi-row CTAs are compiled for <= 256 threads
-    // 16-bit rows of four vectors per thread: the persistent kernel (flags
-    // bit 0: one CTA per row instead), one CTA per resident slot
+    // 16-bit rows of two or four vectors per thread: the persistent kernel
+    // (flags bit 0: one CTA per row instead), one CTA per resident slot
     if constexpr (!std::is_same<T, float>::value) {
-      if (nv == 4 && threads <= 256 && R == 1 && !(cfg && (cfg->flags & 1))) {
-        const bool full = nvec % threads == 0 && nvec / threads == 4;
-        auto kern = full ? rmsnorm_quant_persistent_kernel<T, W, true> : rmsnorm_quant_persistent_kernel<T, W, false>;
+      if ((nv == 2 || nv == 4) && threads <= 256 && R == 1 && !(cfg && (cfg->flags & 1))) {
+        const bool full = nvec % threads == 0 && nvec / threads == nv;
+        auto kern = nv == 4 ? (full ? rmsnorm_quant_persistent_kernel<T, W, true, 4>
+                                    : rmsnorm_quant_persistent_kernel<T, W, false, 4>)
+                            : (full ? rmsnorm_quant_persistent_kernel<T, W, true, 2>
+                                    : rmsnorm_quant_persistent_kernel<T, W, false, 2>);
         int per_sm = 0;
         if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0);
             e != cudaSuccess)
