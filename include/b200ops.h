@@ -270,7 +270,11 @@ int b200_paged_attention_noalloc(const void* q, const void* k_cache,
  * (F16/BF16/F32).  acc_out (nullable): [M, N] int32 raw accumulators.
  * K must be a multiple of 16 and A/W 16-byte aligned.
  * workspace: needed only for split-K (small M); size from
- * b200_int8_gemm_workspace_size().  cfg: tile_n, stages, split. */
+ * b200_int8_gemm_workspace_size().  cfg: M > 128: stages, flags bit 1 (one-SM
+ * kernel, with tile_n 128/256); M <= 64 (streaming kernel): tile_k (bytes of
+ * K per ring stage), stages, tile_m (CTAs of the grid; default n tiles x the
+ * largest k split that fits the SM count), flags bit 2 (split-grid kernel,
+ * with split). */
 size_t b200_int8_gemm_workspace_size(int64_t M, int64_t N, int64_t K,
                                      const b200_launch_cfg* cfg);
 int b200_int8_gemm(const int8_t* A, const int8_t* W, const float* sA,

@@ -285,8 +285,10 @@ const char* b200_query_config_space(const char* op, int64_t rows) {
   } else if (o == "quant_matmul") {
     if (rows > 0 && rows <= 64) {
       kernel = "int8_gemm_stream_kernel";
-      field("tile_k", {0, 128, 256, 512, 1024}, "bytes of K per ring stage (0: 512, 256 for M > 32)");
+      field("tile_k", {0, 128, 256, 384, 512, 1024}, "bytes of K per ring stage (0: 384, 256 for M > 32)");
       field("stages", {0, 4, 6, 8, 10, 12, 14, 16}, "ring depth (0: 16, or as many as fit)");
+      field("tile_m", {0, 64, 96, 112, 128, (int64_t)sms},
+            "CTAs of the grid (0: n tiles x the largest k split within the SM count)");
     } else if (rows > 0 && rows <= 128) {
       kernel = "int8_gemm_tcgen05_kernel";
       field("tile_n", {0, 128, 256}, "output columns per tile (0: 256)");
