@@ -216,6 +216,11 @@ def secondary_ops(dev) -> dict:
     fl = WL.causal_flops(4, 32, 4096, 128)
     res["flash_prefill_causal_B4_H32_T4096_D128"] = {"us": us, "TFLOPs": fl / us / 1e6,
                                                      "frac": fl / us / 1e6 / peaks["bf16_tflops"]}
+    try:  # the library comparator: PyTorch's fused attention (its best available backend)
+        us_sdpa = _median_us(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True), 2, 10)
+        res["flash_prefill_causal_B4_H32_T4096_D128"]["torch_sdpa_TFLOPs"] = fl / us_sdpa / 1e6
+    except Exception:
+        pass
     x, w = WL.rmsnorm_inputs(device=dev)
     y = torch.empty_like(x)
     us = _median_us(lambda: K.rmsnorm(x, w, out=y), flush_l2=True)
@@ -617,8 +622,8 @@ def run_reference(args, ws, rank):
     }
 
 
-PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-skinny", "flash", "rmsnorm", "rmsnorm-quant",
-                 "gemm-gelu", "append-prefill")
+PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-skinny", "flash", "flash-full", "rmsnorm",
+                 "rmsnorm-quant", "gemm-gelu", "append-prefill", "sdpa-full")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -646,6 +651,12 @@ def profile_case(name: str, reps: int = 3) -> None:
     elif name == "flash":
         q, k, v = WL.flash_inputs(B=1, H=8, T=4096, device=dev)
         fn = lambda: K.flash_attn(q, k, v, causal=True)  # noqa: E731
+    elif name in ("flash-full", "sdpa-full"):  # the prefill bench shape, 4 x 32 x 4096 x 128
+        q, k, v = WL.flash_inputs(device=dev)
+        if name == "flash-full":
+            fn = lambda: K.flash_attn(q, k, v, causal=True)  # noqa: E731
+        else:
+            fn = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)  # noqa: E731
     elif name == "rmsnorm-quant":
         x, w = WL.rmsnorm_inputs(device=dev)
         xb, wb = x.bfloat16().reshape(-1, 4096), w.bfloat16()

@@ -270,8 +270,10 @@ int b200_paged_attention_noalloc(const void* q, const void* k_cache,
  * (F16/BF16/F32).  acc_out (nullable): [M, N] int32 raw accumulators.
  * K must be a multiple of 16 and A/W 16-byte aligned.
  * workspace: needed only for split-K (small M); size from
- * b200_int8_gemm_workspace_size().  cfg: M > 128: stages, flags bit 1 (one-SM
- * kernel, with tile_n 128/256); M <= 64 (streaming kernel): tile_k (bytes of
+ * b200_int8_gemm_workspace_size().  cfg: M > 128: stages, tile_n (CTA-pair
+ * tile width 128..256 in steps of 32; default: a wave model that picks 256
+ * unless a narrower width removes a mostly empty wave), flags bit 1 (one-SM kernel, with tile_n
+ * 128/256); M <= 64 (streaming kernel): tile_k (bytes of
  * K per ring stage), stages, tile_m (CTAs of the grid; default n tiles x the
  * largest k split that fits the SM count), flags bit 2 (split-grid kernel,
  * with split). */

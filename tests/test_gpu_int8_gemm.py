@@ -38,7 +38,7 @@ def test_int8_gemm_out_dtypes(out_dtype, cuda_device):
 
 
 # flags bit 1 selects the one-SM persistent kernel over the CTA-pair kernel
-# (the default for M > 128); tile_n applies to the one-SM kernel
+# (the default for M > 128); tile_n is the tile width of either
 @pytest.mark.parametrize("cfg", [{"flags": 2, "tile_n": 128}, {"flags": 2, "tile_n": 256}, {"split": 4},
                                  {"stages": 2}, {"flags": 2, "stages": 3}, {"tile_n": 128, "split": 3, "stages": 3}])
 def test_int8_gemm_configs(cfg, cuda_device):
@@ -54,6 +54,21 @@ def test_int8_gemm_configs(cfg, cuda_device):
 def test_int8_gemm_skinny_kernels(cfg, M, N, K_, cuda_device):
     for seed in (0, 1):
         check(M, N, K_, cuda_device, cfg=cfg, seed=seed)
+
+
+# CTA-pair tile widths (tile_n 128..256, each CTA loading tile_n / 2 W rows;
+# the default picks the width whose tiles fill whole waves of CTA pairs), on
+# ragged N and M, and the streaming kernel's grid size (tile_m)
+@pytest.mark.parametrize("cfg", [{"tile_n": 128}, {"tile_n": 160}, {"tile_n": 192}, {"tile_n": 224}, {"tile_n": 256}])
+@pytest.mark.parametrize("M,N,K_", [(600, 1000, 640), (512, 4096, 1024), (300, 448, 256)])
+def test_int8_gemm_pair_tile_widths(cfg, M, N, K_, cuda_device):
+    check(M, N, K_, cuda_device, cfg=cfg)
+
+
+@pytest.mark.parametrize("cfg", [{"tile_m": 7}, {"tile_m": 64}, {"tile_m": 112}, {"tile_m": 148}, {"tile_m": 1000}])
+def test_int8_gemm_streaming_grid_sizes(cfg, cuda_device):
+    for seed in (0, 1):
+        check(16, 3000, 4096, cuda_device, cfg=cfg, seed=seed)
 
 
 @pytest.mark.parametrize("M,N,K_", [(600, 1000, 640), (257, 300, 128), (129, 256, 4128), (1024, 4096, 48)])

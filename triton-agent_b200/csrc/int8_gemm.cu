@@ -441,13 +441,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 // acc_empty.  No multicast anywhere: every load reads global memory into
 // the issuing CTA's own shared memory.
 // ----------------------------------------------------------------------------
-constexpr int kPairN = 256;
+constexpr int kPairN = 256;  // widest pair tile (and the kind::f16 flavour's)
 
+// TMEM columns for two accumulators of PN columns (allocations are powers of two).
+constexpr uint32_t pair_tmem_cols(int pn) { return 2 * pn <= 256 ? 256u : 512u; }
+
+// PN: output columns of a pair tile (128..256, a multiple of 32; each CTA
+// loads PN / 2 rows of W per stage).  The host picks it per shape so the
+// tiles fill whole waves of CTA pairs.
 // kF16: the bf16/fp16 flavour (kind::f16, fp32 accumulators, B = b [K, N]
 // N-contiguous, i.e. MN-major: per CTA two TMA boxes of 64 N x 64 K, 8 KB
 // apart; epilogue bias + GELU) -- same pipeline, same 32 KB stages, same
 // 32-byte K step per MMA.
-template <typename OutT, bool kF16>
+template <typename OutT, bool kF16, int PN>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                           const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
@@ -476,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // both CTAs' barriers exist before either CTA signals the other's
   sm100::cluster_sync();
   if (warp == 1) {
-    sm100::tmem_alloc_pair(sm100::smem_u32(bars.tmem_slot), 2 * kPairN);
+    sm100::tmem_alloc_pair(sm100::smem_u32(bars.tmem_slot), pair_tmem_cols(PN));
     sm100::tmem_relinquish_pair();
   }
   sm100::tc_fence_before();
@@ -494,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = pair; t < p.num_tiles && ok; t += n_pairs) {
         const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
         const int32_t a_row = m_tile * 2 * BM + (int32_t)rank * BM;
-        const int32_t b_row = n_tile * kPairN + (int32_t)rank * (kPairN / 2);
+        const int32_t b_row = n_tile * PN + (int32_t)rank * (PN / 2);
         for (int kt = 0; kt < p.k_tiles; ++kt, ++it, r.next(p.stages)) {
           const int s = r.s;
           if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[s]), r.ph ^ 1u) || aborted(bars)) {
@@ -526,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // D s32 from s8 x s8, or D f32 from bf16 (1) / fp16 (0) with B MN-major
       constexpr uint32_t ab_fmt = kF16 ? (std::is_same<OutT, __nv_bfloat16>::value ? 1u : 0u) : 1u;
       constexpr uint32_t idesc =
-          sm100::make_idesc(kF16 ? 1u : 2u, ab_fmt, ab_fmt, 0, kF16 ? 1u : 0u, 2 * BM, kPairN);
+          sm100::make_idesc(kF16 ? 1u : 2u, ab_fmt, ab_fmt, 0, kF16 ? 1u : 0u, 2 * BM, PN);
       const uint32_t leader = sm100::elect_one();
       const uint64_t ad0 = sm100::make_smem_desc(base, 16, 1024, sm100::kSwizzle128B);
       // B: K-major (K steps of 32 B inside the atom) or MN-major (the two
@@ -549,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         sm100::tc_fence_after();
-        const uint32_t d_tmem = tmem + a * kPairN;
+        const uint32_t d_tmem = tmem + a * PN;
         for (int kt = 0; kt < p.k_tiles; ++kt, r.next(p.stages)) {
           if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.full[r.s]), r.ph) || aborted(bars)) {
             ok = false;
@@ -591,12 +597,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tc_fence_after();
       const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
       const int64_t row = (int64_t)m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
-      const uint32_t t_row = tmem + a * kPairN + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t t_row = tmem + a * PN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kPairN;) {
-        const int64_t col0 = (int64_t)n_tile * kPairN + c;
+      for (int c = 0; c < PN;) {
+        const int64_t col0 = (int64_t)n_tile * PN + c;
         if constexpr (sizeof(OutT) == 2 && !kF16) {
-          if (p.world > 1 && col0 + kGatherCols <= p.N) {  // warp-uniform
+          if (p.world > 1 && col0 + kGatherCols <= p.N && c + kGatherCols <= PN) {  // warp-uniform
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes);
             c += kGatherCols;
@@ -626,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   sm100::cluster_sync();
   if (warp == 1) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc_pair(tmem, 2 * kPairN);
+    sm100::tmem_dealloc_pair(tmem, pair_tmem_cols(PN));
   }
 }
 
@@ -1048,15 +1054,34 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
     }
   } else if (M > 128 && !(cfg && (cfg->flags & 2)) && sms >= 2) {  // flags bit 1: one-SM persistent kernel
     g.pair = true;
-    g.BN = kPairN;
     g.m_tiles = (int)((M + 2 * BM - 1) / (2 * BM));
-    g.n_tiles = (int)((N + kPairN - 1) / kPairN);
+    const int pairs = sms / 2;
+    // Tile width: tile_n when it is one of 128..256 (step 32), else the one
+    // with the least cost = waves x (width + 224).  A ring stage costs about
+    // its MMA time plus a fixed part as long as the MMA time of a 256-wide
+    // stage (measured: 4096 x 14336 x 4096 took 168 / 169 / 190 / 211 / 247 us
+    // at widths 256 / 224 / 192 / 160 / 128; the ring's bytes in flight are
+    // capped by shared memory, and narrow tiles consume them faster), so
+    // narrower tiles pay off only where they remove a mostly empty wave.
+    int pn = (cfg && cfg->tile_n >= 128 && cfg->tile_n <= 256 && cfg->tile_n % 32 == 0) ? cfg->tile_n : 0;
+    if (pn == 0) {
+      int64_t best = INT64_MAX;
+      for (int cand = kPairN; cand >= 128; cand -= 32) {
+        const int64_t t = (int64_t)g.m_tiles * ((N + cand - 1) / cand);
+        const int64_t cost = ((t + pairs - 1) / pairs) * (cand + 224);
+        if (cost < best) {
+          best = cost;
+          pn = cand;
+        }
+      }
+    }
+    g.BN = pn;
+    g.n_tiles = (int)((N + pn - 1) / pn);
     g.splits = 1;
     g.k_tiles_split = g.k_tiles;
     g.a_bytes = BM * BK;                  // this CTA's 128 rows of A
-    g.stage_bytes = g.a_bytes + (kPairN / 2) * BK;  // + its 128 rows of W
+    g.stage_bytes = g.a_bytes + (pn / 2) * BK;  // + its pn / 2 rows of W
     const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
-    const int pairs = sms / 2;
     g.grid = 2 * (int)(tiles < pairs ? tiles : pairs);
   } else {
     int bn = (cfg && cfg->tile_n > 0) ? cfg->tile_n : 256;
@@ -1072,7 +1097,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
     const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
     g.grid = (int)(tiles < sms ? tiles : sms);
   }
-  g.b_box_rows = g.skinny ? g.BN : (g.pair ? kPairN / 2 : g.BN);
+  g.b_box_rows = g.skinny ? g.BN : (g.pair ? g.BN / 2 : g.BN);
   int stages = (cfg && cfg->stages > 0) ? cfg->stages : (g.stream ? 16 : 8);
   while (stages > 2 && (size_t)stages * g.stage_bytes + bar_bytes(stages) > limit) --stages;
   g.stages = stages;
@@ -1084,7 +1109,19 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
 template <typename OutT, bool kF16>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
                 int32_t* acc_out, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
-  auto kern = int8_gemm_pair_kernel<OutT, kF16>;
+  auto kern = int8_gemm_pair_kernel<OutT, kF16, kPairN>;
+  if constexpr (!kF16) {
+    switch (g.BN) {
+      case 128: kern = int8_gemm_pair_kernel<OutT, kF16, 128>; break;
+      case 160: kern = int8_gemm_pair_kernel<OutT, kF16, 160>; break;
+      case 192: kern = int8_gemm_pair_kernel<OutT, kF16, 192>; break;
+      case 224: kern = int8_gemm_pair_kernel<OutT, kF16, 224>; break;
+      case 256: break;
+      default: return B200_ERR_UNSUPPORTED;
+    }
+  } else if (g.BN != kPairN) {
+    return B200_ERR_UNSUPPORTED;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
   if (e != cudaSuccess) return launch_status(e);
   cudaLaunchConfig_t lc = {};

@@ -297,7 +297,9 @@ const char* b200_query_config_space(const char* op, int64_t rows) {
       kernel = "int8_gemm_pair_kernel";
       field("stages", {0, 2, 3, 4, 5, 6, 7, 8}, "ring depth (0: 8)");
       field("flags", {0, 2}, "2: one-SM persistent kernel (128 x tile_n tiles) instead of CTA pairs");
-      field("tile_n", {0, 128, 256}, "output columns per tile of the one-SM kernel (0: 256)");
+      field("tile_n", {0, 128, 160, 192, 224, 256},
+            "output columns per tile (CTA pairs: 128..256 step 32, 0: a wave model, 256 at the bench shapes; "
+            "one-SM kernel: 128 or 256)");
     }
   } else if (o == "matmul_epilogue") {
     kernel = "int8_gemm_pair_kernel (kind::f16)";
