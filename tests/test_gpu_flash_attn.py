@@ -46,6 +46,30 @@ def test_kernel_variants(cfg, causal, T, S, D, cuda_device):
     check(2, 3, T, S, D, causal, torch.bfloat16, cuda_device, cfg=cfg)
 
 
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("cfg", [None, {"tile_k": 4}, {"flags": 16}])
+def test_running_max_rises_across_key_tiles(causal, cfg, cuda_device):
+    """Keys whose scores grow along the sequence, so the row maximum rises by
+    more than the rescale threshold (2^8) from one key tile to the next: the
+    softmax's P computed from the running max is redone with the new max and
+    O is rescaled; every element against the fp32 oracle."""
+    g = torch.Generator(device=cuda_device).manual_seed(7)
+    B, H, T, D = 1, 4, 1024, 128
+    q = torch.randn(B, H, T, D, generator=g, device=cuda_device)
+    k = torch.randn(B, H, T, D, generator=g, device=cuda_device)
+    k = k * (1.0 + torch.arange(T, device=cuda_device, dtype=torch.float32) / 128.0).view(1, 1, T, 1)
+    q = (q.abs() + 0.5).bfloat16()  # positive queries against growing positive keys
+    k = (k.abs()).bfloat16()
+    # outputs of order 1 (a peaked softmax returns single V rows; bf16 rounds
+    # an output near 4 by up to 0.016 on its own)
+    v = (0.5 * torch.randn(B, H, T, D, generator=g, device=cuda_device)).bfloat16()
+    out = K.flash_attn(q, k, v, causal=causal, cfg=cfg)
+    torch.cuda.synchronize()
+    assert K.read_device_error() == 0
+    exp = O.flash_attn(q.cpu(), k.cpu(), v.cpu(), causal)
+    torch.testing.assert_close(out.cpu().float(), exp, rtol=0, atol=ATOL)
+
+
 def test_golden_reference_cases(golden_dir, cuda_device):
     for c in torch.load(golden_dir / "flash_attn_like.pt"):
         q, k, v = (c[n].bfloat16().to(cuda_device) for n in ("q", "k", "v"))
