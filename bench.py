@@ -622,8 +622,8 @@ def run_reference(args, ws, rank):
     }
 
 
-PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-skinny", "flash", "flash-full", "rmsnorm",
-                 "rmsnorm-quant", "gemm-gelu", "append-prefill", "sdpa-full")
+PROFILE_CASES = ("decode", "decode-split", "append", "gemm", "gemm-cublas", "gemm-skinny", "flash", "flash-full",
+                 "rmsnorm", "rmsnorm-quant", "gemm-gelu", "append-prefill", "sdpa-full")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -644,10 +644,13 @@ def profile_case(name: str, reps: int = 3) -> None:
             cfg = {"flags": 2} if name == "decode-split" else None
             fn = lambda: K.paged_attention(att["q"], cache.k_cache, cache.v_cache, att["block_table"],  # noqa: E731
                                            att["context_len"], cfg=cfg)
-    elif name in ("gemm", "gemm-skinny"):
+    elif name in ("gemm", "gemm-skinny", "gemm-cublas"):
         M = 16 if name == "gemm-skinny" else 4096
         A, W, sA, sW = WL.int8_gemm_inputs(M, 14336, 4096, device=dev)
-        fn = lambda: K.int8_gemm(A, W, sA, sW)  # noqa: E731
+        if name == "gemm-cublas":  # the library comparator on the same operands (int32 out, no dequant)
+            fn = lambda: torch._int_mm(A, W.t())  # noqa: E731
+        else:
+            fn = lambda: K.int8_gemm(A, W, sA, sW)  # noqa: E731
     elif name == "flash":
         q, k, v = WL.flash_inputs(B=1, H=8, T=4096, device=dev)
         fn = lambda: K.flash_attn(q, k, v, causal=True)  # noqa: E731

@@ -1082,7 +1082,10 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
     g.a_bytes = BM * BK;                  // this CTA's 128 rows of A
     g.stage_bytes = g.a_bytes + (pn / 2) * BK;  // + its pn / 2 rows of W
     const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
-    g.grid = 2 * (int)(tiles < pairs ? tiles : pairs);
+    // tile_m: CTA pairs of the grid (default one per two SMs; the tile count
+    // gives one tile per pair, no persistence)
+    const int64_t want = (cfg && cfg->tile_m > 0) ? cfg->tile_m : pairs;
+    g.grid = 2 * (int)(tiles < want ? tiles : want);
   } else {
     int bn = (cfg && cfg->tile_n > 0) ? cfg->tile_n : 256;
     if (bn != 128 && bn != 256) bn = 256;
