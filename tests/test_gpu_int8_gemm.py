@@ -14,16 +14,41 @@ from b200ops.runtime import ops as K
 pytestmark = pytest.mark.gpu
 
 
-def check(M, N, K_, cuda_device, out_dtype=torch.float16, cfg=None, seed=0):
+def check(M, N, K_, cuda_device, out_dtype=torch.float16, cfg=None, seed=0, with_acc=True, sw_offset=0):
+    """Dequantised output bit-exact against the oracle; with_acc also returns
+    the raw int32 accumulators (which routes the tile kernels' epilogue
+    through per-row stores; without them 16-bit outputs go through the
+    staged epilogue).  sw_offset shifts sW by that many floats in its
+    buffer (unaligned scales also take the per-row path)."""
     A, W, sA, sW = WL.int8_gemm_inputs(M, N, K_, device=cuda_device, seed=seed)
-    acc = torch.empty(M, N, dtype=torch.int32, device=cuda_device)
+    if sw_offset:
+        buf = torch.empty(N + sw_offset, dtype=torch.float32, device=cuda_device)
+        buf[sw_offset:] = sW
+        sW = buf[sw_offset:]
+    acc = torch.empty(M, N, dtype=torch.int32, device=cuda_device) if with_acc else None
     C = K.int8_gemm(A, W, sA, sW, out_dtype=out_dtype, acc_out=acc, cfg=cfg)
     torch.cuda.synchronize()
     assert K.read_device_error() == 0
     exp_acc = O.int8_gemm_acc(A.cpu(), W.cpu())
-    assert np.array_equal(acc.cpu().numpy().astype(np.int64), exp_acc)
+    if with_acc:
+        assert np.array_equal(acc.cpu().numpy().astype(np.int64), exp_acc)
     exp = O.dequant(exp_acc, sA.cpu(), sW.cpu(), out_dtype)
     assert torch.equal(C.cpu(), exp)
+
+
+# the staged epilogue (16-bit outputs, no raw accumulators): 128-column groups
+# staged in shared memory and written as whole row runs, ragged edges by rows
+@pytest.mark.parametrize("cfg", [None, {"tile_n": 128}, {"tile_n": 224}, {"flags": 2}, {"flags": 2, "tile_n": 128}])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K_", [(600, 1000, 640), (512, 4096, 1024), (300, 448, 256), (4096, 1280, 128)])
+def test_int8_gemm_staged_epilogue(cfg, out_dtype, M, N, K_, cuda_device):
+    for seed in (0, 1):
+        check(M, N, K_, cuda_device, out_dtype=out_dtype, cfg=cfg, seed=seed, with_acc=False)
+
+
+def test_int8_gemm_unaligned_scales_take_the_row_path(cuda_device):
+    check(600, 1000, 640, cuda_device, with_acc=False, sw_offset=1)
+    check(600, 1000, 640, cuda_device, out_dtype=torch.float32, with_acc=False)
 
 
 @pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (256, 512, 1024), (130, 200, 48), (1, 8, 16),

@@ -62,6 +62,7 @@ struct GemmParams {
   int64_t col_off;
   void* dst[kMaxRanks];
   const void* bias;     // bias + GELU flavour: [N] of the output type
+  int staged;           // tile kernels: 128-column groups through the staged epilogue (gather_group)
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -132,12 +133,17 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row,
   }
 }
 
-// Fused all-gather epilogue for 128 columns of a warp's 32 accumulator rows
-// (16-bit outputs): dequantise in registers, stage [32 rows][128 cols] in
-// the warp's shared buffer, then write it back row by row -- 16 lanes x 16 B,
-// one 256-byte run per row -- into this rank's C and every peer's C.  A warp
-// writing 32 rows x 16 B per instruction would reach the peers as 16-byte
-// NVLink writes; whole rows go as 256-byte runs.
+// Staged epilogue for 128 columns of a warp's 32 accumulator rows (16-bit
+// outputs): dequantise in registers, stage [32 rows][128 cols] in the
+// warp's shared buffer, then write it back row by row -- 16 lanes x 16 B,
+// one 256-byte run per row -- into this rank's C and, for the fused
+// all-gather, every peer's C.  Row-at-a-time stores (each lane its own row,
+// 64 bytes at a time) touch 32 rows per instruction and made the epilogue
+// longer than a short mainloop (4096 x 14336 x 1024: 113 us, staged 76 us;
+// x 4096: 168 -> 145 us); to a peer they arrive as 16-byte NVLink writes.
+// The next 32 columns' TMEM load is in flight while a chunk is dequantised,
+// and the group's 128 column scales are one 16-byte load per lane,
+// broadcast by shuffles.
 constexpr int kGatherCols = 128;
 constexpr int kGatherRowBytes = kGatherCols * 2 + 16;  // +16 B: conflict-free both ways
 constexpr int kGatherWarpBytes = 32 * kGatherRowBytes;
@@ -149,14 +155,21 @@ __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int l
   static_assert(sizeof(OutT) == 2, "staged gather is for 16-bit outputs");
   const int64_t row = row0 + lane;
   const float sa = row < p.M ? sA[row] : 0.f;
-#pragma unroll 1
+  // scales of columns col0 + 4 lane .. col0 + 4 lane + 3 (col0 is 16-byte aligned in sW)
+  const float4 sw4 = __ldg(reinterpret_cast<const float4*>(sW + col0) + lane);
+  uint32_t acc[2][32];
+  sm100::tmem_ld_32x32b_x32(t_row, acc[0]);
+#pragma unroll
   for (int c4 = 0; c4 < kGatherCols / 32; ++c4) {
-    uint32_t acc[32];
-    sm100::tmem_ld_32x32b_x32(t_row + c4 * 32, acc);
-    sm100::tmem_wait_ld_regs(acc);
+    sm100::tmem_wait_ld_regs(acc[c4 & 1]);
+    if (c4 + 1 < kGatherCols / 32) sm100::tmem_ld_32x32b_x32(t_row + (c4 + 1) * 32, acc[(c4 + 1) & 1]);
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = dequant(acc[j], sa, __ldg(&sW[col0 + c4 * 32 + j]));
+    for (int j = 0; j < 32; ++j) {
+      // column c4 * 32 + j: component j % 4 of lane c4 * 8 + j / 4
+      const float mine = (j & 3) == 0 ? sw4.x : (j & 3) == 1 ? sw4.y : (j & 3) == 2 ? sw4.z : sw4.w;
+      v[j] = dequant(acc[c4 & 1][j], sa, __shfl_sync(0xffffffffu, mine, c4 * 8 + (j >> 2)));
+    }
 #pragma unroll
     for (int q = 0; q < 4; ++q)
       *reinterpret_cast<uint4*>(stage + lane * kGatherRowBytes + c4 * 64 + q * 16) = pack16<OutT>(v + 8 * q);
@@ -400,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN;) {
         const int64_t col0 = (int64_t)n_tile * BN + c;
         if constexpr (sizeof(OutT) == 2) {
-          if (p.world > 1 && col0 + kGatherCols <= p.N && c + kGatherCols <= BN) {  // warp-uniform
+          if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= BN) {  // warp-uniform
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes);
             c += kGatherCols;
@@ -602,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < PN;) {
         const int64_t col0 = (int64_t)n_tile * PN + c;
         if constexpr (sizeof(OutT) == 2 && !kF16) {
-          if (p.world > 1 && col0 + kGatherCols <= p.N && c + kGatherCols <= PN) {  // warp-uniform
+          if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= PN) {  // warp-uniform
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes);
             c += kGatherCols;
@@ -999,8 +1012,10 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
   // and empty per stage, 2 + 2 accumulator barriers, mma_done, the TMEM slot
   // and two flags), plus 1 KB of alignment slack
   auto bar_bytes = [](int st) -> size_t { return (size_t)(2 * st + 5) * 8 + 16; };
-  const size_t limit = 227 * 1024 - 1024 - extra_smem;
   g.skinny = M <= 64 && !(cfg && (cfg->flags & 1));  // flags bit 0: force the persistent kernel
+  // extra_smem (the staged epilogue's buffers) belongs to the tile kernels only
+  if (g.skinny) extra_smem = 0;
+  const size_t limit = 227 * 1024 - 1024 - extra_smem;
   if (g.skinny) {
     g.BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     g.m_tiles = 1;
@@ -1211,8 +1226,13 @@ int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* s
   if (ldc < N) return B200_ERR_BAD_ARG;
   if (!aligned16(A) || !aligned16(W)) return B200_ERR_ALIGNMENT;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
-  // fused all-gather: 16 B alignment slack + one staging buffer per epilogue warp
-  const GemmPlan g = plan_gemm(M, N, K, cfg, ga.world > 1 ? 16 + 4 * kGatherWarpBytes : 0);
+  // Staged epilogue (16-bit outputs of the tile kernels, no raw accumulators,
+  // 16-byte aligned scales and output rows): 16 B alignment slack + one
+  // staging buffer per epilogue warp.  The fused all-gather falls back to
+  // per-row stores into every rank's C where these do not hold.
+  const bool staged = dtype_size(out_dtype) == 2 && acc_out == nullptr && aligned16(sW) &&
+                      aligned16(C) && (ldc * 2) % 16 == 0 && (ga.col_off * 2) % 16 == 0;
+  const GemmPlan g = plan_gemm(M, N, K, cfg, staged ? 16 + 4 * kGatherWarpBytes : 0);
   if (g.skinny && (g.splits > 1 || g.stream)) {
     if (workspace == nullptr || workspace_bytes < g.ws_bytes || !aligned16(workspace)) return B200_ERR_WORKSPACE;
     if ((size_t)g.n_tiles * 4 > kTicketBytes) return B200_ERR_UNSUPPORTED;
@@ -1245,6 +1265,7 @@ int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* s
   p.self = ga.self;
   p.col_off = ga.col_off;
   for (int r = 0; r < kMaxRanks; ++r) p.dst[r] = ga.dst[r];
+  p.staged = staged && !g.skinny;
   p.M = M;
   p.N = N;
   p.K = K;
