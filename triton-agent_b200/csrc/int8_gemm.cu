@@ -148,10 +148,15 @@ constexpr int kGatherCols = 128;
 constexpr int kGatherRowBytes = kGatherCols * 2 + 16;  // +16 B: conflict-free both ways
 constexpr int kGatherWarpBytes = 32 * kGatherRowBytes;
 
+// release: when non-zero, the address (shared::cluster) of the accumulator
+// buffer's empty barrier, arrived on as soon as this group's last TMEM load
+// has completed -- the MMA warp may refill the buffer while the rows are
+// still being written out.
 template <typename OutT>
 __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int lane, int64_t col0,
                                              const float* __restrict__ sA, const float* __restrict__ sW,
-                                             OutT* __restrict__ C, const GemmParams& p, uint8_t* stage) {
+                                             OutT* __restrict__ C, const GemmParams& p, uint8_t* stage,
+                                             uint32_t release = 0) {
   static_assert(sizeof(OutT) == 2, "staged gather is for 16-bit outputs");
   const int64_t row = row0 + lane;
   const float sa = row < p.M ? sA[row] : 0.f;
@@ -163,6 +168,11 @@ __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int l
   for (int c4 = 0; c4 < kGatherCols / 32; ++c4) {
     sm100::tmem_wait_ld_regs(acc[c4 & 1]);
     if (c4 + 1 < kGatherCols / 32) sm100::tmem_ld_32x32b_x32(t_row + (c4 + 1) * 32, acc[(c4 + 1) & 1]);
+    if (c4 + 1 == kGatherCols / 32 && release != 0) {
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive_cluster(release);
+    }
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -612,12 +622,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (int64_t)m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
       const uint32_t t_row = tmem + a * PN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
+      bool released = false;
       for (int c = 0; c < PN;) {
         const int64_t col0 = (int64_t)n_tile * PN + c;
         if constexpr (sizeof(OutT) == 2 && !kF16) {
           if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= PN) {  // warp-uniform
+            // the tile's last group hands the accumulator back before its rows go out
+            released = c + kGatherCols == PN;
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
-                               bars.gather + (warp - 2) * kGatherWarpBytes);
+                               bars.gather + (warp - 2) * kGatherWarpBytes, released ? acc_empty0 + a * 8 : 0u);
             c += kGatherCols;
             continue;
           }
@@ -633,9 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         c += 32;
       }
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive_cluster(acc_empty0 + a * 8);
+      if (!released) {
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive_cluster(acc_empty0 + a * 8);
+      }
     }
     // fused all-gather: peer stores visible system-wide before the signal kernel
     if (p.world > 1) __threadfence_system();
