@@ -358,7 +358,7 @@ int b200_quantize_int8(const void* x, int8_t* q, float* scale, int64_t rows,
  * (reference.py:25-28, which assumes T == S).  lse (nullable): [B, H, T] f32
  * natural-log softmax normaliser.  scale <= 0 means 1/sqrt(D).
  * cfg: split (heads per scheduling group, default 8), tile_k (exponential
- * pairs of every 8 computed by a polynomial on the FMA pipe: 1-3, default 1,
+ * pairs of every 8 computed by a polynomial on the FMA pipe: 1-3, default 2,
  * 4 = none); flags: bit 4 persistent kernel, bit 2 two-tile kernel (bit 1
  * with it: polynomial exponentials), bit 0 one-tile kernel. */
 int b200_flash_attn(const void* q, const void* k, const void* v, void* o,

@@ -37,7 +37,7 @@ def check(B, H, T, S, D, causal, dtype, cuda_device, rows=None, seed=0, cfg=None
 # exponentials on the FMA pipe); 1 one-tile kernel.  split: heads per
 # scheduling group.
 # tile_k: exponential pairs (of every 8) on the FMA pipe in the default kernel
-# (0: the default, 1; 4: none)
+# (0: the default, 2; 4: none)
 @pytest.mark.parametrize("cfg", [{"flags": 0}, {"flags": 0, "split": 1}, {"flags": 0, "split": 5}, {"flags": 16},
                                  {"flags": 16, "split": 3}, {"tile_k": 2}, {"tile_k": 3}, {"tile_k": 4}, {"flags": 4},
                                  {"flags": 6}, {"flags": 1}])

@@ -824,32 +824,6 @@ __device__ __forceinline__ float softmax_row_to_tmem(const uint32_t (&v)[kBN], f
   return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
-// Half of softmax_row_to_tmem: 64 scores to 32 packed P pairs in TMEM
-// columns taddr .. taddr + 31; returns their sum.
-template <typename T, int kPoly>
-__device__ __forceinline__ float softmax_half_to_tmem(const uint32_t* v, float sl2, float neg_m, uint32_t taddr) {
-  float s[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) s[i] = 0.f;
-  uint32_t pk[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float x0, x1;
-    sm100::ffma2_bcast(x0, x1, __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), sl2, neg_m);
-    float p0, p1;
-    if ((i & 7) < kPoly) {
-      ex2_poly2(x0, x1, p0, p1);
-    } else {
-      p0 = ex2_approx(x0);
-      p1 = ex2_approx(x1);
-    }
-    sm100::fadd2_acc(s[2 * (i & 3)], s[2 * (i & 3) + 1], p0, p1);
-    pk[i] = pack2<T>(p0, p1);
-  }
-  sm100::tmem_st_32x32b_x32(taddr, pk);
-  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
-}
-
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads3, 1)
     flash_fwd3_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -887,8 +861,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
   uint64_t* s_full = bars + 1 + 2 * kRing3;     // [2 tiles]
   uint64_t* p_full = s_full + 2;                // [2 tiles]
   uint64_t* o_done = s_full + 4;                // [2 tiles]
-  uint64_t* p_half = s_full + 6;                // [2 tiles]: P of the first 64 keys stored
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 6);
   int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
@@ -900,7 +873,6 @@ __global__ void __launch_bounds__(kThreads3, 1)
     for (int i = 0; i < 2; ++i) {
       sm100::mbar_init(sm100::smem_u32(&s_full[i]), 1);
       sm100::mbar_init(sm100::smem_u32(&p_full[i]), 4);
-      sm100::mbar_init(sm100::smem_u32(&p_half[i]), 4);
       sm100::mbar_init(sm100::smem_u32(&o_done[i]), 1);
     }
     *s_abort = 0;
@@ -996,21 +968,14 @@ __global__ void __launch_bounds__(kThreads3, 1)
         sm100::tc_commit(sm100::smem_u32(&s_full[t]), leader);
         return true;
       };
-      // PV in two halves of 64 keys: the first four MMAs start as soon as the
-      // softmax has stored P for the first 64 keys (p_half), while it works
-      // on the second 64 (p_full)
       auto issue_pv = [&](int t, int j, int slot, uint32_t ph) -> bool {
-        if (!sm100::mbar_wait_warp(sm100::smem_u32(&p_half[t]), j & 1)) return false;
+        if (!sm100::mbar_wait_warp(sm100::smem_u32(&p_full[t]), j & 1)) return false;
         if (!sm100::mbar_wait_warp(sm100::smem_u32(&ring_full[slot]), ph)) return false;
         sm100::tc_fence_after();
         const uint64_t bd = dv + (uint64_t)((slot * L::kTile) >> 4);
         const uint32_t d_tmem = tmem + 256 + t * 128, a_tmem = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          if (kk == kBN / 32) {
-            if (!sm100::mbar_wait_warp(sm100::smem_u32(&p_full[t]), j & 1)) return false;
-            sm100::tc_fence_after();
-          }
           // V: MN-major; 16 keys = two 8-row groups of 128 B (SBO 1024),
           // head-dim halves one box (16 KB) apart (LBO).  P: 8 TMEM columns
           // of bf16 pairs per 16 keys.
@@ -1103,8 +1068,15 @@ __global__ void __launch_bounds__(kThreads3, 1)
         rescale = true;
       }
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      float rs;
+      switch (full_tile ? p.poly_pairs : 0) {
+        case 1: rs = softmax_row_to_tmem<T, 1>(v, p.sl2, neg_m, tSt); break;
+        case 2: rs = softmax_row_to_tmem<T, 2>(v, p.sl2, neg_m, tSt); break;
+        case 3: rs = softmax_row_to_tmem<T, 3>(v, p.sl2, neg_m, tSt); break;
+        default: rs = softmax_row_to_tmem<T, 0>(v, p.sl2, neg_m, tSt); break;
+      }
       // O_t holds PV_t(j-1), complete because S_t(j) is: rescale it if the
-      // max moved (before any of P_t(j) is released to the MMA)
+      // max moved (before P_t(j) is released to the MMA)
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
@@ -1121,21 +1093,6 @@ __global__ void __launch_bounds__(kThreads3, 1)
           sm100::tmem_st_32x32b_x32(tOt + c, o);
         }
       }
-      const int poly = full_tile ? p.poly_pairs : 0;
-      auto half = [&](const uint32_t* h, uint32_t taddr) -> float {
-        switch (poly) {
-          case 1: return softmax_half_to_tmem<T, 1>(h, p.sl2, neg_m, taddr);
-          case 2: return softmax_half_to_tmem<T, 2>(h, p.sl2, neg_m, taddr);
-          case 3: return softmax_half_to_tmem<T, 3>(h, p.sl2, neg_m, taddr);
-          default: return softmax_half_to_tmem<T, 0>(h, p.sl2, neg_m, taddr);
-        }
-      };
-      float rs = half(v, tSt);  // keys 0..63 -> P columns [0, 32)
-      sm100::tmem_wait_st();
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(sm100::smem_u32(&p_half[t]));
-      rs += half(v + 64, tSt + 32);  // keys 64..127 -> P columns [32, 64)
       sm100::tmem_wait_st();
       l = l * alpha + rs;
       sm100::tc_fence_before();
@@ -1748,10 +1705,9 @@ extern "C" int b200_flash_attn(const void* q, const void* k, const void* v, void
   p.out_lse = lse != nullptr;
   p.poly_exp = (cfg && (cfg->flags & 2)) ? 1 : 0;  // flags bit 1
   p.head_group = (cfg && cfg->split > 0) ? cfg->split : 8;  // split: heads per scheduling group
-  // tile_k: exponential pairs (of every 8) on the FMA pipe; 0 = default 1
-  // (with P released in two halves: 534 us at B4 H32 T4096 D128 causal
-  // against 543 with two or none), 4 = none
-  p.poly_pairs = ((cfg && cfg->tile_k > 0) ? cfg->tile_k : 1) & 3;
+  // tile_k: exponential pairs (of every 8) on the FMA pipe; 0 = default 2
+  // (measured about 2% faster than none at B4 H32 T4096 D128 causal), 4 = none
+  p.poly_pairs = ((cfg && cfg->tile_k > 0) ? cfg->tile_k : 2) & 3;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc = (D == 64 || D == 128) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) &&
                   B * H <= 0x7fffffffLL && p.n_qt <= 65535 && T < (1ll << 31) && S < (1ll << 31);

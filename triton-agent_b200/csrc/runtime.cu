@@ -307,7 +307,7 @@ const char* b200_query_config_space(const char* op, int64_t rows) {
   } else if (o == "flash_attn_like") {
     kernel = "flash_fwd3_tcgen05_kernel";
     field("split", {0, 1, 2, 4, 8, 16}, "heads per scheduling group sharing K/V in L2 (0: 8)");
-    field("tile_k", {0, 1, 2, 3, 4}, "exponential pairs of every 8 on the FMA pipe (0: 1; 4: none)");
+    field("tile_k", {0, 1, 2, 3, 4}, "exponential pairs of every 8 on the FMA pipe (0: 2; 4: none)");
     field("flags", {0, 16}, "16: persistent kernel (one CTA per SM taking work items)");
   } else {
     return nullptr;
