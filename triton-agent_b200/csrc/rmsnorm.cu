@@ -269,8 +269,8 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
 //    rounding by adding 1.5 * 2^23.
 // The sum of squares is accumulated in the same order as
 // rmsnorm_quant_row_kernel's with one row per CTA of the same size.
-template <typename T, typename W, bool FULL, int NV>
-__global__ void __launch_bounds__(256) rmsnorm_quant_persistent_kernel(
+template <typename T, typename W, bool FULL, int NV, int MAXT>
+__global__ void __launch_bounds__(MAXT, MAXT <= 128 ? 5 : 2) rmsnorm_quant_persistent_kernel(
     const T* __restrict__ x, const W* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ scale,
     T* __restrict__ y, int64_t rows, int D, float eps) {
   constexpr int VN = Vec<T>::N;  // 8
@@ -527,10 +527,14 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     if constexpr (!std::is_same<T, float>::value) {
       if ((nv == 2 || nv == 4) && threads <= 256 && R == 1 && !(cfg && (cfg->flags & 1))) {
         const bool full = nvec % threads == 0 && nvec / threads == nv;
-        auto kern = nv == 4 ? (full ? rmsnorm_quant_persistent_kernel<T, W, true, 4>
-                                    : rmsnorm_quant_persistent_kernel<T, W, false, 4>)
-                            : (full ? rmsnorm_quant_persistent_kernel<T, W, true, 2>
-                                    : rmsnorm_quant_persistent_kernel<T, W, false, 2>);
+        // 128-thread CTAs are compiled for five resident CTAs per SM (at most
+        // 102 registers a thread), larger ones for two
+        auto kern = nv == 4 ? (threads <= 128 ? (full ? rmsnorm_quant_persistent_kernel<T, W, true, 4, 128>
+                                                      : rmsnorm_quant_persistent_kernel<T, W, false, 4, 128>)
+                                              : (full ? rmsnorm_quant_persistent_kernel<T, W, true, 4, 256>
+                                                      : rmsnorm_quant_persistent_kernel<T, W, false, 4, 256>))
+                            : (full ? rmsnorm_quant_persistent_kernel<T, W, true, 2, 256>
+                                    : rmsnorm_quant_persistent_kernel<T, W, false, 2, 256>);
         int per_sm = 0;
         if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0);
             e != cudaSuccess)
