@@ -63,7 +63,24 @@ struct GemmParams {
   void* dst[kMaxRanks];
   const void* bias;     // bias + GELU flavour: [N] of the output type
   int staged;           // tile kernels: 128-column groups through the staged epilogue (gather_group)
+  // CTA-pair kernel work items: items < full_items are whole tiles; the
+  // last partial wave's tiles follow as two half-width items each
+  int full_items, num_items;
 };
+
+// Work item of the CTA-pair kernel: output rows from m_tile, columns
+// [col, col + w) (w = PN, or PN / 2 for a half of a last-wave tile).
+struct PairItem {
+  int m_tile;
+  int64_t col;
+  int w;
+};
+__device__ __forceinline__ PairItem pair_item(const GemmParams& p, int item, int pn) {
+  if (item < p.full_items) return {item % p.m_tiles, (int64_t)(item / p.m_tiles) * pn, pn};
+  const int hi = item - p.full_items;
+  const int t = p.full_items + (hi >> 1);
+  return {t % p.m_tiles, (int64_t)(t / p.m_tiles) * pn + (hi & 1) * (pn / 2), pn / 2};
+}
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -479,8 +496,9 @@ constexpr uint32_t pair_tmem_cols(int pn) { return 2 * pn <= 256 ? 256u : 512u; 
 template <typename OutT, bool kF16, int PN>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                          const float* __restrict__ sA, const float* __restrict__ sW, OutT* __restrict__ C,
-                          int32_t* __restrict__ acc_out, GemmParams p) {
+                          const __grid_constant__ CUtensorMap tm_bh, const float* __restrict__ sA,
+                          const float* __restrict__ sW, OutT* __restrict__ C, int32_t* __restrict__ acc_out,
+                          GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -520,10 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       Ring r;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += n_pairs) {
-        const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
-        const int32_t a_row = m_tile * 2 * BM + (int32_t)rank * BM;
-        const int32_t b_row = n_tile * PN + (int32_t)rank * (PN / 2);
+      for (int t = pair; t < p.num_items && ok; t += n_pairs) {
+        const PairItem itm = pair_item(p, t, PN);
+        const int32_t a_row = itm.m_tile * 2 * BM + (int32_t)rank * BM;
+        const int32_t b_row = (int32_t)itm.col + (int32_t)rank * (itm.w / 2);
+        const CUtensorMap* tmb = itm.w == PN ? &tm_b : &tm_bh;  // half items: boxes of PN / 4 W rows
+        const uint32_t fill_bytes = 2 * (p.a_bytes + (uint32_t)(itm.w / 2) * BK);
         for (int kt = 0; kt < p.k_tiles; ++kt, ++it, r.next(p.stages)) {
           const int s = r.s;
           if (!sm100::mbar_wait(sm100::smem_u32(&bars.empty[s]), r.ph ^ 1u) || aborted(bars)) {
@@ -531,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t fb = sm100::smem_u32(&bars.full[s]);
-          if (rank == 0) sm100::mbar_arrive_expect_tx(fb, 2 * p.stage_bytes);  // both CTAs' fills
+          if (rank == 0) sm100::mbar_arrive_expect_tx(fb, kF16 ? 2 * p.stage_bytes : fill_bytes);  // both CTAs' fills
           const uint32_t fb0 = sm100::mapa_shared(fb, 0);
           const uint32_t dst = base + s * p.stage_bytes;
           if constexpr (kF16) {
@@ -541,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             sm100::tma_load_2d_pair(dst + p.a_bytes + 8192, &tm_b, fb0, b_row + 64, kt * 64);
           } else {
             sm100::tma_load_2d_pair(dst, &tm_a, fb0, kt * BK, a_row);
-            sm100::tma_load_2d_pair(dst + p.a_bytes, &tm_b, fb0, kt * BK, b_row);
+            sm100::tma_load_2d_pair(dst + p.a_bytes, tmb, fb0, kt * BK, b_row);
           }
         }
       }
@@ -556,6 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ab_fmt = kF16 ? (std::is_same<OutT, __nv_bfloat16>::value ? 1u : 0u) : 1u;
       constexpr uint32_t idesc =
           sm100::make_idesc(kF16 ? 1u : 2u, ab_fmt, ab_fmt, 0, kF16 ? 1u : 0u, 2 * BM, PN);
+      constexpr uint32_t idesc_half =
+          sm100::make_idesc(kF16 ? 1u : 2u, ab_fmt, ab_fmt, 0, kF16 ? 1u : 0u, 2 * BM, PN / 2);
       const uint32_t leader = sm100::elect_one();
       const uint64_t ad0 = sm100::make_smem_desc(base, 16, 1024, sm100::kSwizzle128B);
       // B: K-major (K steps of 32 B inside the atom) or MN-major (the two
@@ -570,8 +592,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       Ring r;
       int lt = 0;
       bool ok = true;
-      for (int t = pair; t < p.num_tiles && ok; t += n_pairs, ++lt) {
+      for (int t = pair; t < p.num_items && ok; t += n_pairs, ++lt) {
         const int a = lt & 1;
+        const uint32_t id = t < p.full_items ? idesc : idesc_half;
         // both epilogues must have drained this accumulator (tile lt - 2)
         if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_empty[a]), ((lt >> 1) & 1) ^ 1)) {
           ok = false;
@@ -589,10 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             if constexpr (kF16)
-              sm100::mma_f16_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + b_step * kk, idesc,
+              sm100::mma_f16_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + b_step * kk, id,
                                      (kt > 0 || kk > 0) ? 1u : 0u, leader);
             else
-              sm100::mma_i8_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + b_step * kk, idesc,
+              sm100::mma_i8_ss_pair(d_tmem, ad0 + so + 2 * kk, bd0 + so + b_step * kk, id,
                                     (kt > 0 || kk > 0) ? 1u : 0u, leader);
           }
           sm100::tc_commit_pair(empty_r0 + 8 * r.s, leader);
@@ -611,24 +634,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     int lt = 0;
     const uint32_t acc_empty0 = sm100::mapa_shared(sm100::smem_u32(&bars.acc_empty[0]), 0);
-    for (int t = pair; t < p.num_tiles; t += n_pairs, ++lt) {
+    for (int t = pair; t < p.num_items; t += n_pairs, ++lt) {
       const int a = lt & 1;
       if (!sm100::mbar_wait_warp(sm100::smem_u32(&bars.acc_full[a]), (lt >> 1) & 1)) {
         set_abort(bars, kDevErrTimeoutMma);
         break;
       }
       sm100::tc_fence_after();
-      const int m_tile = t % p.m_tiles, n_tile = t / p.m_tiles;
-      const int64_t row = (int64_t)m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
+      const PairItem itm = pair_item(p, t, PN);
+      const int64_t row = (int64_t)itm.m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
       const uint32_t t_row = tmem + a * PN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
       bool released = false;
-      for (int c = 0; c < PN;) {
-        const int64_t col0 = (int64_t)n_tile * PN + c;
+      for (int c = 0; c < itm.w;) {
+        const int64_t col0 = itm.col + c;
         if constexpr (sizeof(OutT) == 2 && !kF16) {
-          if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= PN) {  // warp-uniform
+          if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= itm.w) {  // warp-uniform
             // the tile's last group hands the accumulator back before its rows go out
-            released = c + kGatherCols == PN;
+            released = c + kGatherCols == itm.w;
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes, released ? acc_empty0 + a * 8 : 0u);
             c += kGatherCols;
@@ -1015,6 +1038,7 @@ struct GemmPlan {
   int b_box_rows;  // rows of the second operand's TMA box
   int BN;  // persistent tile width, or MN (padded M) for skinny
   int splits, k_tiles, k_tiles_split, stages, m_tiles, n_tiles, grid;
+  int full_items, num_items;  // CTA-pair kernel work items (see GemmParams)
   uint32_t stage_bytes, a_bytes;
   size_t smem, ws_bytes;
 };
@@ -1121,6 +1145,16 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
     // gives one tile per pair, no persistence)
     const int64_t want = (cfg && cfg->tile_m > 0) ? cfg->tile_m : pairs;
     g.grid = 2 * (int)(tiles < want ? tiles : want);
+    // The last, partial wave of 256-wide tiles runs as 128-wide halves on
+    // twice the pairs (4096^3: 34 tiles of the fourth wave on 34 of 74 pairs
+    // become 68 halves); flags bit 3 keeps whole tiles.
+    const int64_t np = g.grid / 2;
+    const int64_t rem = np > 0 ? tiles % np : 0;
+    g.full_items = g.num_items = (int)tiles;
+    if (pn == kPairN && rem > 0 && tiles > np && 2 * rem <= np && !(cfg && (cfg->flags & 8))) {
+      g.full_items = (int)(tiles - rem);
+      g.num_items = (int)(tiles + rem);
+    }
   } else {
     int bn = (cfg && cfg->tile_n > 0) ? cfg->tile_n : 256;
     if (bn != 128 && bn != 256) bn = 256;
@@ -1145,8 +1179,9 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, const b200_launch_cfg* cfg, 
 
 // CTA-pair kernel launch: clusters of two CTAs (cudaLaunchKernelEx).
 template <typename OutT, bool kF16>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
-                int32_t* acc_out, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh, const float* sA,
+                const float* sW, void* C, int32_t* acc_out, const GemmPlan& g, const GemmParams& p,
+                cudaStream_t s) {
   auto kern = int8_gemm_pair_kernel<OutT, kF16, kPairN>;
   if constexpr (!kF16) {
     switch (g.BN) {
@@ -1174,15 +1209,15 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, c
   at[0].val.clusterDim.z = 1;
   lc.attrs = at;
   lc.numAttrs = 1;
-  e = cudaLaunchKernelEx(&lc, kern, ta, tb, sA, sW, static_cast<OutT*>(C), acc_out, p);
+  e = cudaLaunchKernelEx(&lc, kern, ta, tb, tbh, sA, sW, static_cast<OutT*>(C), acc_out, p);
   if (e != cudaSuccess) return launch_status(e);
   return launch_status(cudaGetLastError());
 }
 
 template <typename OutT>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const float* sA, const float* sW, void* C,
-           int32_t* acc_out, void* ws, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
-  if (g.pair) return launch_pair<OutT, false>(ta, tb, sA, sW, C, acc_out, g, p, s);
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh, const float* sA, const float* sW,
+           void* C, int32_t* acc_out, void* ws, const GemmPlan& g, const GemmParams& p, cudaStream_t s) {
+  if (g.pair) return launch_pair<OutT, false>(ta, tb, tbh, sA, sW, C, acc_out, g, p, s);
   if (!g.skinny) {
     auto kern = g.BN == 256 ? int8_gemm_tcgen05_kernel<256, OutT> : int8_gemm_tcgen05_kernel<128, OutT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
@@ -1280,12 +1315,24 @@ int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* s
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
+  // W boxes of the CTA-pair kernel's half-width items (a quarter of the tile's rows per CTA)
+  CUtensorMap tbh = tb;
+  if (g.pair && g.num_items > g.full_items) {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)rows1};
+    const uint64_t strides[1] = {(uint64_t)K};
+    const uint32_t box[2] = {BK, (uint32_t)(g.BN / 4)};
+    int st = encode_tensor_map(&tbh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, op1, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
   GemmParams p{};
   p.world = ga.world;
   p.self = ga.self;
   p.col_off = ga.col_off;
   for (int r = 0; r < kMaxRanks; ++r) p.dst[r] = ga.dst[r];
   p.staged = staged && !g.skinny;
+  p.full_items = g.pair ? g.full_items : 0;
+  p.num_items = g.pair ? g.num_items : 0;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -1303,9 +1350,9 @@ int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* s
   p.k_groups = g.k_groups;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (out_dtype) {
-    case B200_F16: return launch<__half>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
-    case B200_BF16: return launch<__nv_bfloat16>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
-    case B200_F32: return launch<float>(ta, tb, sA, sW, C, acc_out, workspace, g, p, s);
+    case B200_F16: return launch<__half>(ta, tb, tbh, sA, sW, C, acc_out, workspace, g, p, s);
+    case B200_BF16: return launch<__nv_bfloat16>(ta, tb, tbh, sA, sW, C, acc_out, workspace, g, p, s);
+    case B200_F32: return launch<float>(ta, tb, tbh, sA, sW, C, acc_out, workspace, g, p, s);
     default: return B200_ERR_UNSUPPORTED;
   }
 }
@@ -1453,10 +1500,11 @@ extern "C" int b200_gemm_bias_gelu(const void* a, const void* b, const void* bia
   p.m_tiles = g.m_tiles;
   p.n_tiles = g.n_tiles;
   p.num_tiles = g.m_tiles * g.n_tiles;
+  p.full_items = p.num_items = p.num_tiles;  // whole tiles only
   p.stage_bytes = g.stage_bytes;
   p.a_bytes = g.a_bytes;
   p.bias = bias;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == B200_BF16) return launch_pair<__nv_bfloat16, true>(ta, tb, nullptr, nullptr, c, nullptr, g, p, s);
-  return launch_pair<__half, true>(ta, tb, nullptr, nullptr, c, nullptr, g, p, s);
+  if (dtype == B200_BF16) return launch_pair<__nv_bfloat16, true>(ta, tb, tb, nullptr, nullptr, c, nullptr, g, p, s);
+  return launch_pair<__half, true>(ta, tb, tb, nullptr, nullptr, c, nullptr, g, p, s);
 }
