@@ -273,7 +273,9 @@ int b200_paged_attention_noalloc(const void* q, const void* k_cache,
  * b200_int8_gemm_workspace_size().  cfg: M > 128: stages, tile_n (CTA-pair
  * tile width 128..256 in steps of 32; default: a wave model that picks 256
  * unless a narrower width removes a mostly empty wave), flags bit 1 (one-SM kernel, with tile_n
- * 128/256); M <= 64 (streaming kernel): tile_k (bytes of
+ * 128/256), flags bit 3 (the last partial wave of 256-wide tiles keeps whole
+ * tiles; by default, when it would busy at most half the CTA pairs, each of
+ * its tiles runs as two 128-wide items); M <= 64 (streaming kernel): tile_k (bytes of
  * K per ring stage), stages, tile_m (CTAs of the grid; default n tiles x the
  * largest k split that fits the SM count), flags bit 2 (split-grid kernel,
  * with split). */

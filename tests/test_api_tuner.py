@@ -60,7 +60,7 @@ def test_axes_are_pruned_to_the_selected_kernel():
     from b200ops.runtime import lib as L
 
     big = dict(_axes(contract("quant_matmul"), L.config_space("quant_matmul", 4096)))
-    assert big["tile_k"] == [0] and big["flags"] == [0, 2] and big["num_stages"] == [0, 4, 6, 8]
+    assert big["tile_k"] == [0] and big["flags"] == [0, 2, 8] and big["num_stages"] == [0, 4, 6, 8]
     small = dict(_axes(contract("quant_matmul"), L.config_space("quant_matmul", 16)))
     assert small["flags"] == [0] and small["tile_n"] == [0] and small["tile_k"] == [0, 256, 1024]
     assert small["num_stages"] == [0, 4, 6, 8, 12] and small["num_warps"] == [0]
@@ -84,11 +84,12 @@ def test_best_of_n_is_seeded_and_planner_threshold():
     a = generate_best_of_n(c, STATE, {"t": None}, n=10, seed=3)
     b = generate_best_of_n(c, STATE, {"t": None}, n=10, seed=3)
     assert [x.to_dict() for _, x in a] == [x.to_dict() for _, x in b]
-    assert plan(c, STATE)["strategy"] == "grid"
-    big = OpContract.from_dict({"op": "x", "inputs": {"a": ["N"]}, "outputs": {"b": ["N"]},
-                                "tolerance": {"max_abs_error": 1, "mean_abs_error": 1},
-                                "search_space": {"split": list(range(20)), "stages": list(range(5))}})
-    assert plan(big, STATE)["strategy"] == "best_of_n"
+    def space(**axes):
+        return OpContract.from_dict({"op": "x", "inputs": {"a": ["N"]}, "outputs": {"b": ["N"]},
+                                     "tolerance": {"max_abs_error": 1, "mean_abs_error": 1}, "search_space": axes})
+    # up to 64 points: the whole grid; above: 64 seeded samples
+    assert plan(space(split=list(range(16)), stages=list(range(4))), STATE) == {"strategy": "grid", "candidates": 64}
+    assert plan(space(split=list(range(20)), stages=list(range(5))), STATE)["strategy"] == "best_of_n"
 
 
 def test_selector_and_promoter():

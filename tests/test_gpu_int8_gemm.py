@@ -47,10 +47,10 @@ def test_int8_gemm_staged_epilogue(cfg, out_dtype, M, N, K_, cuda_device):
 
 
 # the CTA-pair kernel's last partial wave split into half-width items (on 74
-# CTA pairs: 256, 84 and 80 tiles leave 34, 10 and 6 for the last wave);
-# flags bit 3 keeps whole tiles
+# CTA pairs: 256, 84, 80 and 896 tiles leave 34, 10, 6 and 8 for the last
+# wave); flags bit 3 keeps whole tiles
 @pytest.mark.parametrize("cfg", [None, {"flags": 8}])
-@pytest.mark.parametrize("M,N,K_", [(4096, 4096, 256), (1024, 5184, 384), (1024, 5120, 128)])
+@pytest.mark.parametrize("M,N,K_", [(4096, 4096, 256), (1024, 5184, 384), (1024, 5120, 128), (4096, 14336, 128)])
 @pytest.mark.parametrize("with_acc", [True, False])
 def test_int8_gemm_last_wave_halves(cfg, M, N, K_, with_acc, cuda_device):
     check(M, N, K_, cuda_device, cfg=cfg, with_acc=with_acc)

@@ -296,7 +296,9 @@ const char* b200_query_config_space(const char* op, int64_t rows) {
     } else {
       kernel = "int8_gemm_pair_kernel";
       field("stages", {0, 2, 3, 4, 5, 6, 7, 8}, "ring depth (0: 8)");
-      field("flags", {0, 2}, "2: one-SM persistent kernel (128 x tile_n tiles) instead of CTA pairs");
+      field("flags", {0, 2, 8},
+            "2: one-SM persistent kernel (128 x tile_n tiles) instead of CTA pairs; 8: the last partial wave "
+            "keeps whole tiles (0: each of its 256-wide tiles runs as two 128-wide items)");
       field("tile_n", {0, 128, 160, 192, 224, 256},
             "output columns per tile (CTA pairs: 128..256 step 32, 0: a wave model, 256 at the bench shapes; "
             "one-SM kernel: 128 or 256)");
