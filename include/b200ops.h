@@ -119,11 +119,15 @@ int b200_rmsnorm(const void* x, const void* weight, void* y, int64_t rows,
  * One pass over x.  q: [rows, D] int8 (8-byte aligned); scale: [rows]
  * f32; y (nullable): [rows, D] of `dtype`.  Needs D % (16 / sizeof(dtype))
  * == 0 and 16-byte aligned x/weight/y (B200_ERR_ALIGNMENT otherwise).
- * cfg: threads (CTA size, multiple of 32, default about D / 32 for 16-bit
- * dtypes), rows_per_cta (1, 2 or 4 rows per CTA; more than one only with at
- * most 256 threads; default 1); flags bit 0: one CTA per row even where the
- * persistent row loop applies (16-bit rows of four 16-byte vectors per
- * thread, at most 256 threads). */
+ * Default for 16-bit rows of D = 1024, 2048 or 4096: warp rows (one warp a
+ * row, two for 4096; each warp's next row copied into shared memory while
+ * the current one is computed).  cfg: threads (CTA size of the CTA kernels,
+ * multiple of 32, default about D / 32 for 16-bit dtypes; giving it selects
+ * them), rows_per_cta (1, 2 or 4 rows per CTA; more than one only with at
+ * most 256 threads; default 1); flags bit 0: one CTA per row; bit 1: the
+ * persistent CTA row loop (16-bit rows of two or four 16-byte vectors per
+ * thread, at most 256 threads) instead of warp rows; bit 2: warp rows
+ * without the prefetch. */
 int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t* q, float* scale,
                             void* y, int64_t rows, int64_t D, float eps, int32_t dtype,
                             int32_t weight_dtype, const b200_launch_cfg* cfg, void* stream);

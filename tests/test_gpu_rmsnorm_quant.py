@@ -31,11 +31,14 @@ def inputs(rows, D, dtype, wdtype, dev, seed=0):
     (64, 4096, torch.float16, torch.float16), (9, 1000, torch.float32, torch.float32),
     (8 * 2048, 4096, torch.bfloat16, torch.bfloat16), (5, 64, torch.float16, torch.float32),
 ])
-# default (persistent kernel for 16-bit rows of four vectors per thread) /
+# default (warp rows with the next row prefetched into shared memory for
+# 16-bit D = 4096, else the persistent CTA kernel or the row kernel) / warp
+# rows without the prefetch (flags 4) / the persistent CTA kernel (flags 2) /
 # one CTA per row (flags 1) / b200_rmsnorm's CTA size for D=4096, with 1, 2
 # and 4 rows per CTA
-@pytest.mark.parametrize("cfg", [None, {"flags": 1}, {"threads": 256}, {"threads": 256, "flags": 1},
-                                 {"rows_per_cta": 4}, {"threads": 128, "rows_per_cta": 2}])
+@pytest.mark.parametrize("cfg", [None, {"flags": 4}, {"flags": 2}, {"flags": 1}, {"threads": 256},
+                                 {"threads": 256, "flags": 1}, {"rows_per_cta": 4},
+                                 {"threads": 128, "rows_per_cta": 2}])
 def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
     x, w = inputs(rows, D, dtype, wdtype, cuda_device)
     q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg=cfg)
@@ -64,19 +67,24 @@ def test_bit_identical_to_unfused(rows, D, dtype, wdtype, cfg, cuda_device):
     assert torch.equal(q2, q) and torch.equal(s2, s)
 
 
-@pytest.mark.parametrize("rows,D", [(1, 4096), (7, 8192), (300, 1024), (2048, 4104)])
+@pytest.mark.parametrize("rows,D", [(1, 4096), (7, 8192), (300, 1024), (2048, 4104), (2048, 4096),
+                                    (5000, 1024), (3001, 2048), (4099, 4096)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_persistent_kernel_row_loop_and_tails(rows, D, dtype, cuda_device):
-    """The persistent kernel's row loop (fewer CTAs than rows, the next row
-    prefetched), partial last vectors (D not a multiple of the CTA's
-    vectors), widths whose codes land on +-127 and rows that are all zero:
-    codes exactly the oracle quantiser's on the kernel's y, and equal to the
-    one-CTA-per-row kernel's."""
+@pytest.mark.parametrize("cfg", [None, {"flags": 2}, {"flags": 4}])
+def test_row_loops_and_tails(rows, D, dtype, cfg, cuda_device):
+    """The row loops of the warp-row kernel (with and without the shared-
+    memory prefetch; several rows per warp group once rows exceed the
+    resident groups, which the larger cases force) and of the persistent CTA
+    kernel (fewer CTAs than rows, the next row prefetched in registers);
+    partial last vectors (D not a multiple of the CTA's vectors), widths
+    whose codes land on +-127 and rows that are all zero: codes exactly the
+    oracle quantiser's on the kernel's y, and equal to the one-CTA-per-row
+    kernel's."""
     x, w = inputs(rows, D, dtype, dtype, cuda_device, seed=rows)
     x[0, :] = 0
     if rows > 3:
         x[3, :] = x[3, :].abs()  # one-signed row: the maximum lands exactly on 127
-    q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True)
+    q, s, y = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg=cfg)
     q1, s1, y1 = K.rmsnorm_quant_int8(x, w, 1e-6, want_y=True, cfg={"flags": 1})
     torch.cuda.synchronize()
     q_o, s_o = O.quantize_int8(y.cpu())

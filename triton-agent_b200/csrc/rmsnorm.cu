@@ -248,6 +248,54 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
   }
 }
 
+// INT8 codes of eight 16-bit values y (one 16-byte vector of T's bits) for
+// the row scale s, rs = RN(1/s):
+//  - bf16: q = RN_bf16(y * rs) without Markstein's correction.  y and s
+//    have 8-bit significands, so y / s is either exactly representable in
+//    bf16 or a fraction p/q (q odd, q <= 255) at least 2^-17 (relative) away
+//    from every bf16 rounding midpoint; y * rs is within 2^-23 of y / s, so
+//    both round to the same bf16 value (and the fp32 rounding of the
+//    quotient, which the reference performs first, cannot land on a
+//    midpoint either).  fp16's 11-bit significands leave no such margin, so
+//    fp16 keeps the corrected quotient;
+//  - the clamp to [-127, 127] is one min.xorsign.abs on the packed pair
+//    (rint commutes with clamping at an integer), before the integer
+//    rounding by adding 1.5 * 2^23 to each widened half: the low byte of the
+//    sum's bits is rint(v) as int8.
+template <typename T>
+__device__ __forceinline__ uint2 quant_vec8(const uint4& yv, float s, float rs) {
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
+  uint32_t h[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float v0, v1;
+    if constexpr (kBF16) {
+      const float y0 = __uint_as_float(yw[k] << 16), y1 = __uint_as_float(yw[k] & 0xFFFF0000u);
+      float q0, q1;
+      sm100::fmul2_bcast(q0, q1, y0, y1, rs);
+      uint32_t pk;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(q1), "f"(q0));
+      asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x42FE42FEu));  // +-127
+      asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.bf16 %0, l, %3; add.rn.f32.bf16 %1, h, %3; }"
+          : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
+    } else {
+      const float2 yf = __half22float2(*reinterpret_cast<const __half2*>(&yw[k]));
+      float q0, q1, e0, e1;
+      sm100::fmul2_bcast(q0, q1, yf.x, yf.y, rs);
+      sm100::ffma2(e0, e1, q0, q1, -s, -s, yf.x, yf.y);
+      sm100::ffma2(v0, v1, e0, e1, rs, rs, q0, q1);
+      uint32_t pk;
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(v1), "f"(v0));
+      asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x57F057F0u));  // +-127
+      asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.f16 %0, l, %3; add.rn.f32.f16 %1, h, %3; }"
+          : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
+    }
+    h[k] = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x0040);
+  }
+  return make_uint2(__byte_perm(h[0], h[1], 0x5410), __byte_perm(h[2], h[3], 0x5410));
+}
+
 // Persistent variant for 16-bit rows of NV = 2 or 4 vectors per thread: a grid of the resident CTA count loops
 // over rows, so the weights are widened to fp32 once per CTA and kept in
 // registers, and the next row's x is loaded while the current row is reduced
@@ -256,17 +304,7 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
 //  - max|y| is taken on the fp32 products before their rounding to T (the
 //    rounding is monotonic, so the rounded maximum is the maximum of the
 //    rounded values) instead of re-widening the rounded row;
-//  - bf16: q = RN_bf16(y * RN(1/s)) without Markstein's correction.  y and s
-//    have 8-bit significands, so y / s is either exactly representable in
-//    bf16 or a fraction p/q (q odd, q <= 255) at least 2^-17 (relative) away
-//    from every bf16 rounding midpoint; y * RN(1/s) is within 2^-23 of y / s,
-//    so both round to the same bf16 value (and the fp32 rounding of the
-//    quotient, which the reference performs first, cannot land on a
-//    midpoint either).  fp16's 11-bit significands leave no such margin, so
-//    fp16 keeps the corrected quotient;
-//  - the clamp to [-127, 127] is one min.xorsign.abs on the packed pair
-//    (rint commutes with clamping at an integer), before the integer
-//    rounding by adding 1.5 * 2^23.
+//  - the codes come from quant_vec8 (bf16 without Markstein's correction).
 // The sum of squares is accumulated in the same order as
 // rmsnorm_quant_row_kernel's with one row per CTA of the same size.
 template <typename T, typename W, bool FULL, int NV, int MAXT>
@@ -274,7 +312,6 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 128 ? 5 : 2) rmsnorm_quant_persi
     const T* __restrict__ x, const W* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ scale,
     T* __restrict__ y, int64_t rows, int D, float eps) {
   constexpr int VN = Vec<T>::N;  // 8
-  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   __shared__ float red[32], red2[32];
   const int nvec = D / VN;
   const int tid = threadIdx.x, nt = blockDim.x;
@@ -350,45 +387,137 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 128 ? 5 : 2) rmsnorm_quant_persi
     if (tid == 0) scale[r] = s;
     int8_t* qr = q + r * D;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if (!live(i)) continue;
-      const uint32_t* yw = reinterpret_cast<const uint32_t*>(&cur[i]);
-      uint32_t h[VN / 2];
-#pragma unroll
-      for (int k = 0; k < VN / 2; ++k) {
-        float v0, v1;
-        if constexpr (kBF16) {
-          const float y0 = __uint_as_float(yw[k] << 16), y1 = __uint_as_float(yw[k] & 0xFFFF0000u);
-          float q0, q1;
-          sm100::fmul2_bcast(q0, q1, y0, y1, rs);
-          uint32_t pk;
-          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(q1), "f"(q0));
-          asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x42FE42FEu));  // +-127
-          // widen each half and add 1.5 * 2^23 in one mixed-precision add:
-          // the low byte of the sum's bits is rint(v) as int8
-          asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.bf16 %0, l, %3; add.rn.f32.bf16 %1, h, %3; }"
-              : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
-        } else {
-          const float2 yf = __half22float2(*reinterpret_cast<const __half2*>(&yw[k]));
-          float q0, q1, e0, e1;
-          sm100::fmul2_bcast(q0, q1, yf.x, yf.y, rs);
-          sm100::ffma2(e0, e1, q0, q1, -s, -s, yf.x, yf.y);
-          sm100::ffma2(v0, v1, e0, e1, rs, rs, q0, q1);
-          uint32_t pk;
-          asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(v1), "f"(v0));
-          asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x57F057F0u));  // +-127
-          asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.f16 %0, l, %3; add.rn.f32.f16 %1, h, %3; }"
-              : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
-        }
-        h[k] = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x0040);
-      }
-      uint2 pk2;
-      pk2.x = __byte_perm(h[0], h[1], 0x5410);
-      pk2.y = __byte_perm(h[2], h[3], 0x5410);
-      *reinterpret_cast<uint2*>(qr + (int64_t)(tid + i * nt) * VN) = pk2;
-    }
+    for (int i = 0; i < NV; ++i)
+      if (live(i)) *reinterpret_cast<uint2*>(qr + (int64_t)(tid + i * nt) * VN) = quant_vec8<T>(cur[i], s, rs);
 #pragma unroll
     for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+  }
+}
+
+// SPLIT warps per row (1 or 2), for 16-bit rows of D = 256 NVW SPLIT: lane
+// l of the group's warp h holds the row's 16-byte vectors h 32 NVW + l +
+// 32 i (NVW of them; each warp load one contiguous 512-byte run), so the
+// reductions are warp shuffles plus, for two warps, one exchange through
+// shared memory under a 64-thread named barrier; no CTA-wide barrier
+// separates a row's phases, and the groups of an SM run their rows
+// independently, some loading while others compute.  The weights are
+// widened to fp32 once per CTA into shared memory (elements 0-3 and 4-7 of
+// each vector in two arrays, so a warp's 16-byte reads are conflict-free).
+// Rows are strided over the grid's groups; the host sizes the grid so that
+// every group takes the same number of rows, give or take one.  Per
+// element: the persistent kernel's arithmetic (max|y| before rounding,
+// quant_vec8 codes) with the sum of squares in a different fp32 order.
+template <typename T, typename W, int NVW, int SPLIT, bool PF>
+__global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
+    const T* __restrict__ x, const W* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ scale,
+    T* __restrict__ y, int64_t rows, float eps) {
+  static_assert(SPLIT == 1 || SPLIT == 2, "one or two warps per row");
+  constexpr int VN = Vec<T>::N;  // 8
+  constexpr int NVEC = 32 * NVW * SPLIT;
+  constexpr int D = NVEC * VN;
+  constexpr int kGroups = 4 / SPLIT;  // row groups of a 128-thread CTA
+  __shared__ float4 wlo[NVEC], whi[NVEC];
+  __shared__ float xch[2][kGroups][SPLIT];
+  // PF: each warp's next row is copied into shared memory (two buffers of
+  // its NVW x 32 vectors) while the current one is computed
+  extern __shared__ uint4 xbuf[];
+  uint4* mybuf = xbuf + (threadIdx.x >> 5) * 2 * NVW * 32;
+  for (int v = threadIdx.x; v < NVEC; v += blockDim.x) {
+    float wf[VN];
+    load_weights<W, VN>(w + (int64_t)v * VN, wf);
+    wlo[v] = make_float4(wf[0], wf[1], wf[2], wf[3]);
+    whi[v] = make_float4(wf[4], wf[5], wf[6], wf[7]);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = warp / SPLIT, half = warp % SPLIT;
+  const int vb = half * 32 * NVW + lane;  // this lane's first vector
+  const int64_t ng = (int64_t)gridDim.x * kGroups;
+  // both warps of a group take the same rows, so they meet at every barrier
+  auto pair_sync = [&] {
+    if constexpr (SPLIT == 2) {
+      if (grp == 0)
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+      else
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+    }
+  };
+  auto prefetch = [&](int64_t rr, int b) {
+    const T* src = x + rr * D + (int64_t)vb * VN;
+#pragma unroll
+    for (int i = 0; i < NVW; ++i) {
+      const uint32_t dst = sm100::smem_u32(mybuf + b * NVW * 32 + lane + 32 * i);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + i * 32 * VN) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  int buf = 0;
+  if constexpr (PF) {
+    const int64_t r0 = (int64_t)blockIdx.x * kGroups + grp;
+    if (r0 < rows) prefetch(r0, 0);
+  }
+  for (int64_t r = (int64_t)blockIdx.x * kGroups + grp; r < rows; r += ng) {
+    uint4 u[NVW];
+    if constexpr (PF) {
+      // each lane reads back only the 16-byte slots it copied itself
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+      for (int i = 0; i < NVW; ++i) u[i] = mybuf[buf * NVW * 32 + lane + 32 * i];
+      if (r + ng < rows) prefetch(r + ng, buf ^ 1);
+      buf ^= 1;
+    } else {
+      const T* xr = x + r * D + (int64_t)vb * VN;
+#pragma unroll
+      for (int i = 0; i < NVW; ++i) u[i] = ldg_stream16(xr + i * 32 * VN);
+    }
+    float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NVW; ++i) {
+      float f[VN];
+      unpack16<T>(u[i], f);
+#pragma unroll
+      for (int j = 0; j < VN; j += 2) sm100::ffma2(ss0, ss1, f[j], f[j + 1], f[j], f[j + 1], ss0, ss1);
+    }
+    float ss = warp_sum(ss0 + ss1);  // xor butterfly: the same bits in every lane
+    if constexpr (SPLIT == 2) {
+      if (lane == 0) xch[0][grp][half] = ss;
+      pair_sync();
+      ss = xch[0][grp][0] + xch[0][grp][1];
+    }
+    // ss / D: D = 2^k divides exactly as a multiply by 2^-k
+    constexpr bool kPow2 = (D & (D - 1)) == 0;
+    const float ms = kPow2 ? ss * (1.0f / D) : __fdiv_rn(ss, (float)D);
+    const float rstd = 1.0f / sqrtf(__fadd_rn(ms, eps));
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < NVW; ++i) {
+      float f[VN];
+      unpack16<T>(u[i], f);
+      const float4 a = wlo[vb + 32 * i], b = whi[vb + 32 * i];
+      const float wf[VN] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < VN; j += 2) {
+        sm100::fmul2_bcast(f[j], f[j + 1], f[j], f[j + 1], rstd);
+        sm100::fmul2(f[j], f[j + 1], f[j], f[j + 1], wf[j], wf[j + 1]);
+        amax = sm100::fmax3(amax, fabsf(f[j]), fabsf(f[j + 1]));
+      }
+      u[i] = pack16<T>(f);  // y rounded to T
+      if (y != nullptr) stg_stream16(y + r * D + (int64_t)(vb + 32 * i) * VN, u[i]);
+    }
+    asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(amax) : "f"(amax));
+    if constexpr (SPLIT == 2) {
+      // the sum slot of this row was read before either warp arrives here,
+      // and the next row's is written after this barrier: two slots suffice
+      if (lane == 0) xch[1][grp][half] = amax;
+      pair_sync();
+      amax = fmaxf(xch[1][grp][0], xch[1][grp][1]);
+    }
+    const float s = finish_scale<T>(round_to<T>(amax));
+    const float rs = __frcp_rn(s);
+    if (lane == 0 && half == 0) scale[r] = s;
+    int8_t* qr = q + r * D + (int64_t)vb * VN;
+#pragma unroll
+    for (int i = 0; i < NVW; ++i) *reinterpret_cast<uint2*>(qr + i * 32 * VN) = quant_vec8<T>(u[i], s, rs);
   }
 }
 
@@ -506,6 +635,7 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
       return B200_ERR_ALIGNMENT;
     const int64_t nvec = D / VN;
     int threads = (cfg && cfg->threads > 0) ? cfg->threads : 0;
+    const int threads_given = threads;
     if (threads != 0 && (threads < 32 || threads > 1024 || threads % 32 != 0)) return B200_ERR_BAD_ARG;
     if (threads == 0) {
       // about four 16-byte vectors per thread (measured best for D = 4096)
@@ -522,9 +652,39 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     int R = (cfg && cfg->rows_per_cta > 0) ? cfg->rows_per_cta : kQuantRowsPerCta;
     if (R != 1 && R != 2 && R != 4) return B200_ERR_BAD_ARG;
     if (nv > 4 || threads > 256) R = 1;  // multi-row CTAs are compiled for <= 256 threads
-    // 16-bit rows of two or four vectors per thread: the persistent kernel
-    // (flags bit 0: one CTA per row instead), one CTA per resident slot
+    // otherwise, 16-bit rows of two or four vectors per thread: the
+    // persistent CTA kernel (flags bit 0: one CTA per row instead), one CTA
+    // per resident slot
     if constexpr (!std::is_same<T, float>::value) {
+      // warp rows for D = 1024, 2048 (one warp a row) and 4096 (two), unless
+      // a CTA size is given or flags bit 0 or 1 asks for the CTA kernels;
+      // flags bit 2: no shared-memory prefetch of the next row
+      const int fl = cfg ? cfg->flags : 0;
+      if ((D == 1024 || D == 2048 || D == 4096) && threads_given == 0 && R == 1 && !(fl & 3)) {
+        const bool pf = !(fl & 4);
+        auto kern = D == 4096 ? (pf ? rmsnorm_quant_warp_kernel<T, W, 8, 2, true> : rmsnorm_quant_warp_kernel<T, W, 8, 2, false>)
+                  : D == 2048 ? (pf ? rmsnorm_quant_warp_kernel<T, W, 8, 1, true> : rmsnorm_quant_warp_kernel<T, W, 8, 1, false>)
+                              : (pf ? rmsnorm_quant_warp_kernel<T, W, 4, 1, true> : rmsnorm_quant_warp_kernel<T, W, 4, 1, false>);
+        const int groups_per_cta = D == 4096 ? 2 : 4;
+        // two row buffers per warp (NVW x 32 16-byte vectors each)
+        const int dyn = pf ? 4 * 2 * (D == 1024 ? 4 : 8) * 32 * 16 : 0;
+        if (dyn > 0) {
+          if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+              e != cudaSuccess)
+            return launch_status(e);
+        }
+        int per_sm = 0;
+        if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, dyn); e != cudaSuccess)
+          return launch_status(e);
+        if (per_sm < 1) per_sm = 1;
+        // every group the same number of rows (n), give or take one
+        const int64_t max_groups = (int64_t)per_sm * device_sm_count() * groups_per_cta;
+        const int64_t n = (rows + max_groups - 1) / max_groups;
+        const int64_t groups = (rows + n - 1) / n;
+        kern<<<(unsigned)((groups + groups_per_cta - 1) / groups_per_cta), 128, dyn, s>>>(xp, wp, q, scale, yp, rows,
+                                                                                            eps);
+        return launch_status(cudaGetLastError());
+      }
       if ((nv == 2 || nv == 4) && threads <= 256 && R == 1 && !(cfg && (cfg->flags & 1))) {
         const bool full = nvec % threads == 0 && nvec / threads == nv;
         // 128-thread CTAs are compiled for five resident CTAs per SM (at most

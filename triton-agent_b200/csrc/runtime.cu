@@ -141,6 +141,8 @@ const char* b200_kernel_list(void) {
   return "rmsnorm_row_kernel\n"
          "rmsnorm_loop_kernel\n"
          "rmsnorm_quant_row_kernel\n"
+         "rmsnorm_quant_persistent_kernel\n"
+         "rmsnorm_quant_warp_kernel\n"
          "rope_kernel\n"
          "kv_scatter_kernel\n"
          "rope_kv_append_paged_kernel\n"
@@ -256,10 +258,14 @@ const char* b200_query_config_space(const char* op, int64_t rows) {
     kernel = "rmsnorm_row_kernel";
     field("threads", {0, 128, 256, 512, 1024}, "CTA size (0: 256, or fewer for short rows)");
   } else if (o == "rmsnorm_quant") {
-    kernel = "rmsnorm_quant_row_kernel";
-    field("threads", {0, 64, 128, 256, 512, 1024}, "CTA size (0: about four 16-byte vectors per thread)");
-    field("rows_per_cta", {0, 1, 2, 4}, "rows per CTA (0: 1; more than 1 only with <= 256 threads)");
-    field("flags", {0, 1}, "1: one CTA per row instead of the persistent row loop (16-bit rows)");
+    kernel = "rmsnorm_quant_warp_kernel";
+    field("threads", {0, 64, 128, 256, 512, 1024},
+          "CTA size of the CTA kernels (0: warp rows for 16-bit D = 1024, 2048, 4096, else about four 16-byte "
+          "vectors per thread)");
+    field("rows_per_cta", {0, 1, 2, 4}, "rows per CTA of the CTA kernels (0: 1; more than 1 only with <= 256 threads)");
+    field("flags", {0, 1, 2, 4},
+          "1: one CTA per row; 2: the persistent CTA row loop instead of warp rows; 4: warp rows without the "
+          "shared-memory prefetch of the next row");
   } else if (o == "rope") {
     kernel = "rope_kernel";
     field("threads", {0, 64, 128, 256}, "CTA size, at most 256 (0: 256)");
