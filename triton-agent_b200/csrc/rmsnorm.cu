@@ -260,8 +260,9 @@ __global__ void __launch_bounds__(R == 1 ? 1024 : 256) rmsnorm_quant_row_kernel(
 //    fp16 keeps the corrected quotient;
 //  - the clamp to [-127, 127] is one min.xorsign.abs on the packed pair
 //    (rint commutes with clamping at an integer), before the integer
-//    rounding by adding 1.5 * 2^23 to each widened half: the low byte of the
-//    sum's bits is rint(v) as int8.
+//    rounding: bf16 adds 1.5 * 2^23 to each widened half (the low byte of
+//    the sum's bits is rint(v) as int8), fp16 adds 1.5 * 2^10 to the packed
+//    pair.
 template <typename T>
 __device__ __forceinline__ uint2 quant_vec8(const uint4& yv, float s, float rs) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -288,12 +289,18 @@ __device__ __forceinline__ uint2 quant_vec8(const uint4& yv, float s, float rs) 
       uint32_t pk;
       asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(pk) : "f"(v1), "f"(v0));
       asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(pk) : "r"(pk), "r"(0x57F057F0u));  // +-127
-      asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.f16 %0, l, %3; add.rn.f32.f16 %1, h, %3; }"
-          : "=f"(v0), "=f"(v1) : "r"(pk), "f"(12582912.0f));
+      // + 1536 (1.5 * 2^10) in f16x2: the sums lie in [1409, 1663], where
+      // the fp16 spacing is 1, so the add rounds v half to even and the low
+      // byte of each half's bits (0x6600 + rint(v)) is rint(v) as int8
+      asm("add.rn.f16x2 %0, %1, %2;" : "=r"(h[k]) : "r"(pk), "r"(0x66006600u));
+      continue;
     }
     h[k] = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x0040);
   }
-  return make_uint2(__byte_perm(h[0], h[1], 0x5410), __byte_perm(h[2], h[3], 0x5410));
+  if constexpr (kBF16)
+    return make_uint2(__byte_perm(h[0], h[1], 0x5410), __byte_perm(h[2], h[3], 0x5410));
+  else  // codes in bytes 0 and 2 of each word
+    return make_uint2(__byte_perm(h[0], h[1], 0x6420), __byte_perm(h[2], h[3], 0x6420));
 }
 
 // Persistent variant for 16-bit rows of NV = 2 or 4 vectors per thread: a grid of the resident CTA count loops
@@ -418,10 +425,10 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
   constexpr int kGroups = 4 / SPLIT;  // row groups of a 128-thread CTA
   __shared__ float4 wlo[NVEC], whi[NVEC];
   __shared__ float xch[2][kGroups][SPLIT];
-  // PF: each warp's next row is copied into shared memory (two buffers of
+  // PF: each warp's next row is copied into shared memory (one buffer of
   // its NVW x 32 vectors) while the current one is computed
   extern __shared__ uint4 xbuf[];
-  uint4* mybuf = xbuf + (threadIdx.x >> 5) * 2 * NVW * 32;
+  uint4* mybuf = xbuf + (threadIdx.x >> 5) * NVW * 32;
   for (int v = threadIdx.x; v < NVEC; v += blockDim.x) {
     float wf[VN];
     load_weights<W, VN>(w + (int64_t)v * VN, wf);
@@ -442,19 +449,21 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
         asm volatile("bar.sync 2, 64;" ::: "memory");
     }
   };
-  auto prefetch = [&](int64_t rr, int b) {
+  // dep: a value computed from everything this lane read from the buffer,
+  // so the copies that refill it issue only after those reads returned
+  auto prefetch = [&](int64_t rr, uint32_t dep) {
     const T* src = x + rr * D + (int64_t)vb * VN;
 #pragma unroll
     for (int i = 0; i < NVW; ++i) {
-      const uint32_t dst = sm100::smem_u32(mybuf + b * NVW * 32 + lane + 32 * i);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + i * 32 * VN) : "memory");
+      const uint32_t dst = sm100::smem_u32(mybuf + lane + 32 * i);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + i * 32 * VN), "r"(dep)
+                   : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  int buf = 0;
   if constexpr (PF) {
     const int64_t r0 = (int64_t)blockIdx.x * kGroups + grp;
-    if (r0 < rows) prefetch(r0, 0);
+    if (r0 < rows) prefetch(r0, 0u);
   }
   for (int64_t r = (int64_t)blockIdx.x * kGroups + grp; r < rows; r += ng) {
     uint4 u[NVW];
@@ -462,9 +471,7 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
       // each lane reads back only the 16-byte slots it copied itself
       asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
-      for (int i = 0; i < NVW; ++i) u[i] = mybuf[buf * NVW * 32 + lane + 32 * i];
-      if (r + ng < rows) prefetch(r + ng, buf ^ 1);
-      buf ^= 1;
+      for (int i = 0; i < NVW; ++i) u[i] = mybuf[lane + 32 * i];
     } else {
       const T* xr = x + r * D + (int64_t)vb * VN;
 #pragma unroll
@@ -479,6 +486,11 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
       for (int j = 0; j < VN; j += 2) sm100::ffma2(ss0, ss1, f[j], f[j + 1], f[j], f[j + 1], ss0, ss1);
     }
     float ss = warp_sum(ss0 + ss1);  // xor butterfly: the same bits in every lane
+    if constexpr (PF) {
+      // the next row's copies overlap the rest of this one; the buffer is
+      // refilled only after every value read from it fed ss
+      if (r + ng < rows) prefetch(r + ng, __float_as_uint(ss));
+    }
     if constexpr (SPLIT == 2) {
       if (lane == 0) xch[0][grp][half] = ss;
       pair_sync();
@@ -666,8 +678,8 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
                   : D == 2048 ? (pf ? rmsnorm_quant_warp_kernel<T, W, 8, 1, true> : rmsnorm_quant_warp_kernel<T, W, 8, 1, false>)
                               : (pf ? rmsnorm_quant_warp_kernel<T, W, 4, 1, true> : rmsnorm_quant_warp_kernel<T, W, 4, 1, false>);
         const int groups_per_cta = D == 4096 ? 2 : 4;
-        // two row buffers per warp (NVW x 32 16-byte vectors each)
-        const int dyn = pf ? 4 * 2 * (D == 1024 ? 4 : 8) * 32 * 16 : 0;
+        // a row buffer per warp (NVW x 32 16-byte vectors)
+        const int dyn = pf ? 4 * (D == 1024 ? 4 : 8) * 32 * 16 : 0;
         if (dyn > 0) {
           if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
               e != cudaSuccess)
