@@ -407,22 +407,24 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 128 ? 5 : 2) rmsnorm_quant_persi
 // reductions are warp shuffles plus, for two warps, one exchange through
 // shared memory under a 64-thread named barrier; no CTA-wide barrier
 // separates a row's phases, and the groups of an SM run their rows
-// independently, some loading while others compute.  The weights are
-// widened to fp32 once per CTA into shared memory (elements 0-3 and 4-7 of
-// each vector in two arrays, so a warp's 16-byte reads are conflict-free).
+// independently, some loading while others compute.  One 512-thread CTA
+// per SM (16 warps) widens the weights to fp32 once into shared memory
+// (elements 0-3 and 4-7 of each vector in two arrays, so a warp's 16-byte
+// reads are conflict-free); four 128-thread CTAs, each with its own copy,
+// ran 5% slower.
 // Rows are strided over the grid's groups; the host sizes the grid so that
 // every group takes the same number of rows, give or take one.  Per
 // element: the persistent kernel's arithmetic (max|y| before rounding,
 // quant_vec8 codes) with the sum of squares in a different fp32 order.
 template <typename T, typename W, int NVW, int SPLIT, bool PF>
-__global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
+__global__ void __launch_bounds__(512, 1) rmsnorm_quant_warp_kernel(
     const T* __restrict__ x, const W* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ scale,
     T* __restrict__ y, int64_t rows, float eps) {
   static_assert(SPLIT == 1 || SPLIT == 2, "one or two warps per row");
   constexpr int VN = Vec<T>::N;  // 8
   constexpr int NVEC = 32 * NVW * SPLIT;
   constexpr int D = NVEC * VN;
-  constexpr int kGroups = 4 / SPLIT;  // row groups of a 128-thread CTA
+  constexpr int kGroups = 16 / SPLIT;  // row groups of a 512-thread CTA
   __shared__ float4 wlo[NVEC], whi[NVEC];
   __shared__ float xch[2][kGroups][SPLIT];
   // PF: each warp's next row is copied into shared memory (one buffer of
@@ -443,10 +445,7 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_quant_warp_kernel(
   // both warps of a group take the same rows, so they meet at every barrier
   auto pair_sync = [&] {
     if constexpr (SPLIT == 2) {
-      if (grp == 0)
-        asm volatile("bar.sync 1, 64;" ::: "memory");
-      else
-        asm volatile("bar.sync 2, 64;" ::: "memory");
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + grp) : "memory");  // barriers 1..8
     }
   };
   // dep: a value computed from everything this lane read from the buffer,
@@ -677,23 +676,23 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
         auto kern = D == 4096 ? (pf ? rmsnorm_quant_warp_kernel<T, W, 8, 2, true> : rmsnorm_quant_warp_kernel<T, W, 8, 2, false>)
                   : D == 2048 ? (pf ? rmsnorm_quant_warp_kernel<T, W, 8, 1, true> : rmsnorm_quant_warp_kernel<T, W, 8, 1, false>)
                               : (pf ? rmsnorm_quant_warp_kernel<T, W, 4, 1, true> : rmsnorm_quant_warp_kernel<T, W, 4, 1, false>);
-        const int groups_per_cta = D == 4096 ? 2 : 4;
+        const int groups_per_cta = D == 4096 ? 8 : 16;
         // a row buffer per warp (NVW x 32 16-byte vectors)
-        const int dyn = pf ? 4 * (D == 1024 ? 4 : 8) * 32 * 16 : 0;
+        const int dyn = pf ? 16 * (D == 1024 ? 4 : 8) * 32 * 16 : 0;
         if (dyn > 0) {
           if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
               e != cudaSuccess)
             return launch_status(e);
         }
         int per_sm = 0;
-        if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, dyn); e != cudaSuccess)
+        if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 512, dyn); e != cudaSuccess)
           return launch_status(e);
         if (per_sm < 1) per_sm = 1;
         // every group the same number of rows (n), give or take one
         const int64_t max_groups = (int64_t)per_sm * device_sm_count() * groups_per_cta;
         const int64_t n = (rows + max_groups - 1) / max_groups;
         const int64_t groups = (rows + n - 1) / n;
-        kern<<<(unsigned)((groups + groups_per_cta - 1) / groups_per_cta), 128, dyn, s>>>(xp, wp, q, scale, yp, rows,
+        kern<<<(unsigned)((groups + groups_per_cta - 1) / groups_per_cta), 512, dyn, s>>>(xp, wp, q, scale, yp, rows,
                                                                                             eps);
         return launch_status(cudaGetLastError());
       }
