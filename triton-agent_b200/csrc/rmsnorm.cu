@@ -1,4 +1,5 @@
-// RMSNorm, y = x * rsqrt(mean(x^2) + eps) * w, one CTA per row.
+// RMSNorm, y = x * rsqrt(mean(x^2) + eps) * w, and RMSNorm fused with the
+// row INT8 quantiser of the next GEMM's activations.
 //
 // Reference: triton_agent/ops/rmsnorm/reference.py:17-18.
 //
@@ -663,9 +664,6 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
     int R = (cfg && cfg->rows_per_cta > 0) ? cfg->rows_per_cta : kQuantRowsPerCta;
     if (R != 1 && R != 2 && R != 4) return B200_ERR_BAD_ARG;
     if (nv > 4 || threads > 256) R = 1;  // multi-row CTAs are compiled for <= 256 threads
-    // otherwise, 16-bit rows of two or four vectors per thread: the
-    // persistent CTA kernel (flags bit 0: one CTA per row instead), one CTA
-    // per resident slot
     if constexpr (!std::is_same<T, float>::value) {
       // warp rows for D = 1024, 2048 (one warp a row) and 4096 (two), unless
       // a CTA size is given or flags bit 0 or 1 asks for the CTA kernels;
@@ -696,6 +694,9 @@ extern "C" int b200_rmsnorm_quant_int8(const void* x, const void* weight, int8_t
                                                                                             eps);
         return launch_status(cudaGetLastError());
       }
+      // otherwise, 16-bit rows of two or four vectors per thread: the
+      // persistent CTA kernel (flags bit 0: one CTA per row instead), one CTA
+      // per resident slot
       if ((nv == 2 || nv == 4) && threads <= 256 && R == 1 && !(cfg && (cfg->flags & 1))) {
         const bool full = nvec % threads == 0 && nvec / threads == nv;
         // 128-thread CTAs are compiled for five resident CTAs per SM (at most
