@@ -257,6 +257,24 @@ def secondary_ops(dev) -> dict:
     nb = WL.append_bytes(16384, HQ, HKV, D)
     res["rope_kv_append_paged_prefill_16384tok"] = {"us": us, "GBps": nb / us / 1e3,
                                                     "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    # quant_matmul through the reference interface (ops/quant_matmul cuda_v1: per-row quantiser of a,
+    # per-column quantiser of b with the transposed K-major output, INT8 GEMM, fp32 out), and its two
+    # quantisers alone
+    from b200ops.ops.quant_matmul.templates import cuda_v1 as qm
+    g = torch.Generator(device=dev).manual_seed(13)
+    a_q = torch.randn(1, 4096, 4096, generator=g, device=dev).bfloat16()
+    b_q = torch.randn(4096, 14336, generator=g, device=dev).bfloat16()
+    us = _median_us(lambda: K.quantize_int8(a_q.reshape(4096, 4096)), flush_l2=True)
+    nb = 4096 * 4096 * 3 + 4096 * 4
+    res["quantize_int8_rows_bf16_4096x4096"] = {"us": us, "GBps": nb / us / 1e3, "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    us = _median_us(lambda: K.quantize_int8(b_q, by_column=True), flush_l2=True)
+    nb = 4096 * 14336 * 3 + 14336 * 4
+    res["quantize_int8_cols_bf16_4096x14336"] = {"us": us, "GBps": nb / us / 1e3,
+                                                  "frac": nb / us / 1e3 / peaks["hbm_gbs"]}
+    fn = qm.sm100()
+    us = _median_us(lambda: fn(a_q, b_q), flush_l2=True)
+    res["quant_matmul_op_bf16_1x4096x4096_x_4096x14336"] = {
+        "us": us, "includes": "both quantisers + INT8 GEMM with fp32 output, as the reference op"}
     return res
 
 

@@ -24,6 +24,26 @@ def test_quantize_codes_exact(dtype, shape, by_column, cuda_device):
     assert torch.equal(s.cpu(), es.float())
 
 
+# the packed 16-bit paths: warp rows (widths of at most 4096, multiples of 8)
+# and 64-column strips over a cluster of four CTAs (rows a multiple of 16;
+# 32 and 16 rows leave CTAs of the cluster without rows)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape,by_column", [((16, 64), True), ((32, 128), True), ((1040, 320), True),
+                                             ((4096, 1024), True), ((5, 8), False), ((9, 4088), False),
+                                             ((4100, 2048), False)])
+def test_packed_paths_codes_exact(dtype, shape, by_column, cuda_device):
+    g = torch.Generator().manual_seed(shape[0] + 3 * shape[1])
+    x = (torch.randn(*shape, generator=g) * torch.exp2(torch.randint(-6, 6, (shape[0], 1), generator=g).float()))
+    x = x.to(dtype)
+    x[0] = 0
+    x[:, 1] = 0  # a zero column: scale -> 1e-6
+    q, s = K.quantize_int8(x.to(cuda_device), by_column=by_column)
+    torch.cuda.synchronize()
+    eq, es = O.quantize_int8(x, by_column=by_column)
+    assert torch.equal(s.cpu(), es.float().reshape(-1))
+    assert torch.equal(q.cpu(), eq)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 def test_quantize_codes_exact_at_scale_and_ties(dtype, cuda_device):
     """2048 rows x 4096: random rows of many magnitudes, and rows whose scale
@@ -42,5 +62,11 @@ def test_quantize_codes_exact_at_scale_and_ties(dtype, cuda_device):
     x = x.to(dtype)
     q, s = K.quantize_int8(x.to(cuda_device))
     eq, es = O.quantize_int8(x)
+    assert torch.equal(s.cpu(), es.float().reshape(-1))
+    assert torch.equal(q.cpu(), eq)
+    # the same values as columns (4096 rows x 2048 columns: the strip path for 16-bit types)
+    xt = x.t().contiguous()
+    q, s = K.quantize_int8(xt.to(cuda_device), by_column=True)
+    eq, es = O.quantize_int8(xt, by_column=True)
     assert torch.equal(s.cpu(), es.float().reshape(-1))
     assert torch.equal(q.cpu(), eq)

@@ -9,11 +9,169 @@
 // common.cuh), so the int8 codes are bit-identical.  The scale is returned as fp32 (exact widening of
 // the dtype-rounded value).
 #include "common.cuh"
+#include "quant.cuh"
+#include "sm100.cuh"
 
 namespace b200 {
 namespace {
 
-// One CTA per row.
+// 16-bit rows of at most 4096 elements (a multiple of 8), one warp per row:
+// the row's 16-byte vectors stay in registers (lane l holds vectors l,
+// l + 32, ...) between the packed absolute maximum and the codes
+// (quant_vec8, bit-identical to quant_code_fast).
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_warp_kernel(const T* __restrict__ x, int8_t* __restrict__ q,
+                                                                 float* __restrict__ scale, int64_t rows,
+                                                                 int64_t cols) {
+  constexpr int NV = 16;  // vectors per lane: 16 x 32 x 8 = 4096 elements
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;  // warp-uniform
+  const int nvec = (int)(cols / 8);
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * cols);
+  uint4 u[NV];
+  uint32_t m0 = 0u, m1 = 0u;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = lane + 32 * i;
+    u[i] = v < nvec ? ldg_stream16(xr + v) : make_uint4(0u, 0u, 0u, 0u);
+    m0 = absmax2<T>(m0, absmax2<T>(u[i].x, u[i].y));
+    m1 = absmax2<T>(m1, absmax2<T>(u[i].z, u[i].w));
+  }
+  float a = fmaxf(absmax_of_pair<T>(m0), absmax_of_pair<T>(m1));
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(a) : "f"(a));
+  const float s = finish_scale<T>(a);
+  const float rs = __frcp_rn(s);
+  if (lane == 0) scale[r] = s;
+  int8_t* qr = q + r * cols;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) *reinterpret_cast<uint2*>(qr + (int64_t)v * 8) = quant_vec8<T>(u[i], s, rs);
+  }
+}
+
+// Per-column quantisation with the transposed output q [cols, rows] (the
+// INT8 GEMM's weight operand): a cluster of kColSplit CTAs covers a strip of
+// 64 columns, each CTA a contiguous range of rows_per rows.  Pass 1: the
+// column maxima of the CTA's rows (16-byte loads, 8 lanes a row, packed
+// absolute maxima), combined over the cluster through distributed shared
+// memory.  Pass 2 (the CTA's rows again, mostly from L2): 128-row tiles
+// staged in shared memory, so that a thread quantises runs of 16 rows of one
+// column with quant_vec8 and writes each as one 16-byte run of q.  Needs
+// cols % 64 == 0, rows % 16 == 0 and 16-byte aligned x and q.
+constexpr int kColSplit = 4;
+
+template <typename T>
+__global__ void __cluster_dims__(1, kColSplit, 1) __launch_bounds__(256)
+    quantize_cols_strip_kernel(const T* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scale,
+                               int64_t rows, int64_t cols, int64_t rows_per) {
+  __shared__ __align__(16) uint4 tile[128 * 8];  // 128 rows x 64 columns of T
+  __shared__ uint32_t red[8][32];               // per warp: packed maxima of the strip's 64 columns
+  __shared__ uint32_t part[32];                 // this CTA's maxima, read by the whole cluster
+  __shared__ float s_s[64], s_r[64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * 64;
+  const int64_t rb = (int64_t)blockIdx.y * rows_per;
+  const int64_t re = rb + rows_per < rows ? rb + rows_per : rows;
+  const int cg = lane & 7, rl = lane >> 3;
+  // ---- pass 1: word j of a lane's maxima holds columns 2j, 2j + 1 of its 8-column group
+  // eight rows of loads in flight per thread
+  uint32_t m[4] = {0u, 0u, 0u, 0u};
+  for (int64_t r = rb + warp * 4 + rl; r < re; r += 32 * 8) {
+    uint4 u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      u[k] = r + 32 * k < re ? __ldg(reinterpret_cast<const uint4*>(x + (r + 32 * k) * cols + c0) + cg)
+                             : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      m[0] = absmax2<T>(m[0], u[k].x);
+      m[1] = absmax2<T>(m[1], u[k].y);
+      m[2] = absmax2<T>(m[2], u[k].z);
+      m[3] = absmax2<T>(m[3], u[k].w);
+    }
+  }
+#pragma unroll
+  for (int o = 8; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = absmax2<T>(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+  if (rl == 0)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp][cg * 4 + i] = m[i];
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t w = red[0][tid];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) w = absmax2<T>(w, red[k][tid]);
+    part[tid] = w;
+  }
+  sm100::cluster_sync();  // every CTA's part is written
+  if (tid < 32) {
+    uint32_t w = 0u;
+#pragma unroll
+    for (int k = 0; k < kColSplit; ++k) {
+      uint32_t pw;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];"
+                   : "=r"(pw)
+                   : "r"(sm100::mapa_shared(sm100::smem_u32(&part[tid]), (uint32_t)k))
+                   : "memory");
+      w = absmax2<T>(w, pw);
+    }
+    const uint32_t mm = w & 0x7FFF7FFFu;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t bits = h ? (mm >> 16) : (mm & 0xFFFFu);
+      float a;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        a = __uint_as_float(bits << 16);
+      else
+        a = __half2float(__ushort_as_half((unsigned short)bits));
+      const float sv = finish_scale<T>(a);
+      s_s[2 * tid + h] = sv;
+      s_r[2 * tid + h] = __frcp_rn(sv);
+      if (blockIdx.y == 0) scale[c0 + 2 * tid + h] = sv;
+    }
+  }
+  sm100::cluster_sync();  // no CTA leaves while a peer may still read its part; s_s / s_r visible
+  // ---- pass 2: 128-row tiles; the next tile's loads are in flight (in
+  // registers) while the current one is quantised from shared memory
+  const int c = tid & 63, rg = tid >> 6;  // column, 32-row group of the tile
+  const float sc = s_s[c], rc = s_r[c];
+  const uint16_t* t16 = reinterpret_cast<const uint16_t*>(tile);
+  auto load_tile = [&](int64_t r0, uint4 (&pre)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = tid + 256 * k;  // row e / 8, 8-column group e % 8
+      const int64_t r = r0 + (e >> 3);
+      pre[k] = r < re ? __ldg(reinterpret_cast<const uint4*>(x + r * cols + c0) + (e & 7))
+                      : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  uint4 pre[4];
+  if (rb < re) load_tile(rb, pre);
+  for (int64_t r0 = rb; r0 < re; r0 += 128) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tile[tid + 256 * k] = pre[k];
+    __syncthreads();
+    if (r0 + 128 < re) load_tile(r0 + 128, pre);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int tr = rg * 32 + h * 16;  // first tile row of this 16-row run
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        w[i] = (uint32_t)t16[(tr + 2 * i) * 64 + c] | ((uint32_t)t16[(tr + 2 * i + 1) * 64 + c] << 16);
+      const uint2 qa = quant_vec8<T>(make_uint4(w[0], w[1], w[2], w[3]), sc, rc);
+      const uint2 qb = quant_vec8<T>(make_uint4(w[4], w[5], w[6], w[7]), sc, rc);
+      const int64_t rr0 = r0 + tr;
+      if (rr0 < re) *reinterpret_cast<uint4*>(q + (c0 + c) * rows + rr0) = make_uint4(qa.x, qa.y, qb.x, qb.y);
+    }
+    __syncthreads();
+  }
+}
+
+// General path (any width and dtype): one CTA per row.
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x,
                                                             int8_t* __restrict__ q,
@@ -41,7 +199,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) qr[i] = (int8_t)quant_code_fast<T>(to_f32(xr[i]), s, rs);
 }
 
-// One CTA per 32 columns of x [rows, cols]; writes q transposed [cols, rows].
+// General path: one CTA per 32 columns of x [rows, cols]; writes q transposed [cols, rows].
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_cols_kernel(const T* __restrict__ x,
                                                             int8_t* __restrict__ q,
@@ -100,6 +258,22 @@ extern "C" int b200_quantize_int8(const void* x, int8_t* q, float* scale, int64_
   if (!x || !q || !scale) return B200_ERR_BAD_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return B200_DISPATCH_FLOAT(dtype, [&] {
+    constexpr bool k16 = !std::is_same<scalar_t, float>::value;
+    if (k16 && !by_column && cols % 8 == 0 && cols <= 4096 && aligned16(x) &&
+        reinterpret_cast<uintptr_t>(q) % 8 == 0 && rows <= 8LL * 0x7fffffffLL) {
+      // packed warp rows (16-byte vectors held in registers)
+      quantize_rows_warp_kernel<scalar_t><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(
+          static_cast<const scalar_t*>(x), q, scale, rows, cols);
+      return launch_status(cudaGetLastError());
+    }
+    if (k16 && by_column && cols % 64 == 0 && rows % 16 == 0 && aligned16(x) && aligned16(q) &&
+        cols / 64 <= 0x7fffffffLL) {
+      // column strips of 64, each over a cluster of kColSplit CTAs
+      const int64_t rows_per = ((rows + kColSplit - 1) / kColSplit + 127) / 128 * 128;
+      quantize_cols_strip_kernel<scalar_t><<<dim3((unsigned)(cols / 64), kColSplit), 256, 0, s>>>(
+          static_cast<const scalar_t*>(x), q, scale, rows, cols, rows_per);
+      return launch_status(cudaGetLastError());
+    }
     if (!by_column) {
       if (rows > 0x7fffffffLL) return (int)B200_ERR_UNSUPPORTED;
       quantize_rows_kernel<scalar_t><<<(unsigned)rows, 256, 0, s>>>(

@@ -158,7 +158,9 @@ const char* b200_kernel_list(void) {
          "int8_gemm_skinny_kernel\n"
          "peer_flag_exchange_kernel\n"
          "quantize_rows_kernel\n"
+         "quantize_rows_warp_kernel\n"
          "quantize_cols_kernel\n"
+         "quantize_cols_strip_kernel\n"
          "flash_fwd3_tcgen05_kernel\n"
          "flash_fwd4_persistent_kernel\n"
          "flash_fwd2_tcgen05_kernel\n"
