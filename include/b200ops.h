@@ -356,8 +356,9 @@ int b200_ipc_close(void* dev_ptr, int64_t offset);
  * 16-bit x takes packed paths when it can: rows of at most 4096 elements (a
  * multiple of 8, x 16-byte and q 8-byte aligned) one warp per row; columns
  * (cols % 64 == 0, rows % 16 == 0, x and q 16-byte aligned) 64-column strips
- * over clusters of four CTAs.  Everything else (and fp32) takes the general
- * kernels; the codes are the same on every path. */
+ * over clusters of eight CTAs holding their rows in shared memory (up to
+ * 4096 rows) or of four CTAs reading x twice.  Everything else (and fp32)
+ * takes the general kernels; the codes are the same on every path. */
 int b200_quantize_int8(const void* x, int8_t* q, float* scale, int64_t rows,
                        int64_t cols, int32_t dtype, int32_t by_column,
                        const b200_launch_cfg* cfg, void* stream);

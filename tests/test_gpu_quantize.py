@@ -25,12 +25,13 @@ def test_quantize_codes_exact(dtype, shape, by_column, cuda_device):
 
 
 # the packed 16-bit paths: warp rows (widths of at most 4096, multiples of 8)
-# and 64-column strips over a cluster of four CTAs (rows a multiple of 16;
-# 32 and 16 rows leave CTAs of the cluster without rows)
+# and 64-column strips (rows a multiple of 16) over a cluster of eight CTAs
+# holding their rows in shared memory (up to 4096 rows; 32 and 16 rows leave
+# CTAs of the cluster without rows) or, above, of four CTAs reading x twice
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("shape,by_column", [((16, 64), True), ((32, 128), True), ((1040, 320), True),
-                                             ((4096, 1024), True), ((5, 8), False), ((9, 4088), False),
-                                             ((4100, 2048), False)])
+                                             ((4096, 1024), True), ((4112, 128), True), ((8192, 64), True),
+                                             ((5, 8), False), ((9, 4088), False), ((4100, 2048), False)])
 def test_packed_paths_codes_exact(dtype, shape, by_column, cuda_device):
     g = torch.Generator().manual_seed(shape[0] + 3 * shape[1])
     x = (torch.randn(*shape, generator=g) * torch.exp2(torch.randint(-6, 6, (shape[0], 1), generator=g).float()))

@@ -243,6 +243,112 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(const T* __restrict_
   }
 }
 
+// Per-column quantisation for at most 4096 rows, x read from DRAM once: a
+// cluster of kColSplitR CTAs covers a strip of 64 columns, each CTA up to
+// 512 rows, which it keeps in shared memory (64 KB) between the packed
+// column maxima (combined over the cluster through distributed shared
+// memory, as in quantize_cols_strip_kernel) and the codes (a thread
+// quantises 32 rows of one column per step and writes them as two 16-byte
+// runs, a whole 32-byte sector of q).  Needs cols % 64 == 0, rows % 16 == 0 and 16-byte aligned x and q.
+constexpr int kColSplitR = 8;
+constexpr int kResidentRows = 512;
+
+template <typename T>
+__global__ void __cluster_dims__(1, kColSplitR, 1) __launch_bounds__(256)
+    quantize_cols_resident_kernel(const T* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scale,
+                                  int64_t rows, int64_t cols, int rows_per) {
+  extern __shared__ __align__(16) uint4 rtile[];  // rows_per rows x 64 columns of T
+  __shared__ uint32_t red[8][32];
+  __shared__ uint32_t part[32];
+  __shared__ float s_s[64], s_r[64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * 64;
+  const int64_t rb = (int64_t)blockIdx.y * rows_per;
+  const int n = rb < rows ? (int)((rows - rb) < rows_per ? (rows - rb) : rows_per) : 0;  // rows of this CTA
+  const int cg = tid & 7;  // the thread's 8-column group: element e = tid + 256 k has e % 8 == cg
+  // ---- pass 1: the CTA's rows into shared memory, eight 16-byte loads in flight per thread
+  uint32_t m[4] = {0u, 0u, 0u, 0u};
+  for (int e0 = 0; e0 < n * 8; e0 += 256 * 8) {
+    uint4 u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = e0 + tid + 256 * k;
+      u[k] = e < n * 8 ? __ldg(reinterpret_cast<const uint4*>(x + (rb + (e >> 3)) * cols + c0) + cg)
+                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = e0 + tid + 256 * k;
+      if (e < n * 8) rtile[e] = u[k];
+      m[0] = absmax2<T>(m[0], u[k].x);
+      m[1] = absmax2<T>(m[1], u[k].y);
+      m[2] = absmax2<T>(m[2], u[k].z);
+      m[3] = absmax2<T>(m[3], u[k].w);
+    }
+  }
+#pragma unroll
+  for (int o = 8; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = absmax2<T>(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+  if (lane < 8)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp][cg * 4 + i] = m[i];
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t w = red[0][tid];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) w = absmax2<T>(w, red[k][tid]);
+    part[tid] = w;
+  }
+  sm100::cluster_sync();  // every CTA's part is written
+  if (tid < 32) {
+    uint32_t w = 0u;
+#pragma unroll
+    for (int k = 0; k < kColSplitR; ++k) {
+      uint32_t pw;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];"
+                   : "=r"(pw)
+                   : "r"(sm100::mapa_shared(sm100::smem_u32(&part[tid]), (uint32_t)k))
+                   : "memory");
+      w = absmax2<T>(w, pw);
+    }
+    const uint32_t mm = w & 0x7FFF7FFFu;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t bits = h ? (mm >> 16) : (mm & 0xFFFFu);
+      float a;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        a = __uint_as_float(bits << 16);
+      else
+        a = __half2float(__ushort_as_half((unsigned short)bits));
+      const float sv = finish_scale<T>(a);
+      s_s[2 * tid + h] = sv;
+      s_r[2 * tid + h] = __frcp_rn(sv);
+      if (blockIdx.y == 0) scale[c0 + 2 * tid + h] = sv;
+    }
+  }
+  sm100::cluster_sync();  // no CTA leaves while a peer may still read its part; tile, s_s, s_r visible
+  // ---- pass 2: the codes from shared memory, 32 rows of one column per
+  // thread and step (whole 32-byte sectors of q)
+  const int c = tid & 63, rg = tid >> 6;
+  const float sc = s_s[c], rc = s_r[c];
+  const uint16_t* t16 = reinterpret_cast<const uint16_t*>(rtile);
+  for (int t0 = rg * 32; t0 < n; t0 += 128) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int tr = t0 + 16 * h;
+      if (tr >= n) break;
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        w[i] = (uint32_t)t16[(tr + 2 * i) * 64 + c] | ((uint32_t)t16[(tr + 2 * i + 1) * 64 + c] << 16);
+      const uint2 qa = quant_vec8<T>(make_uint4(w[0], w[1], w[2], w[3]), sc, rc);
+      const uint2 qb = quant_vec8<T>(make_uint4(w[4], w[5], w[6], w[7]), sc, rc);
+      *reinterpret_cast<uint4*>(q + (c0 + c) * rows + rb + tr) = make_uint4(qa.x, qa.y, qb.x, qb.y);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace b200
 
@@ -264,6 +370,21 @@ extern "C" int b200_quantize_int8(const void* x, int8_t* q, float* scale, int64_
       // packed warp rows (16-byte vectors held in registers)
       quantize_rows_warp_kernel<scalar_t><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(
           static_cast<const scalar_t*>(x), q, scale, rows, cols);
+      return launch_status(cudaGetLastError());
+    }
+    if (k16 && by_column && cols % 64 == 0 && rows % 16 == 0 && aligned16(x) && aligned16(q) &&
+        cols / 64 <= 0x7fffffffLL && rows <= (int64_t)kColSplitR * kResidentRows) {
+      // up to 4096 rows: column strips held in shared memory, x read once
+      const int rows_per = (int)(((rows + kColSplitR - 1) / kColSplitR + 15) / 16 * 16);
+      const int dyn = rows_per * 128;
+      auto kern = quantize_cols_resident_kernel<scalar_t>;
+      if (dyn > 48 * 1024) {
+        if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+            e != cudaSuccess)
+          return launch_status(e);
+      }
+      kern<<<dim3((unsigned)(cols / 64), kColSplitR), 256, dyn, s>>>(static_cast<const scalar_t*>(x), q, scale,
+                                                                     rows, cols, rows_per);
       return launch_status(cudaGetLastError());
     }
     if (k16 && by_column && cols % 64 == 0 && rows % 16 == 0 && aligned16(x) && aligned16(q) &&

@@ -161,6 +161,7 @@ const char* b200_kernel_list(void) {
          "quantize_rows_warp_kernel\n"
          "quantize_cols_kernel\n"
          "quantize_cols_strip_kernel\n"
+         "quantize_cols_resident_kernel\n"
          "flash_fwd3_tcgen05_kernel\n"
          "flash_fwd4_persistent_kernel\n"
          "flash_fwd2_tcgen05_kernel\n"
