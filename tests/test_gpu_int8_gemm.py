@@ -17,8 +17,8 @@ pytestmark = pytest.mark.gpu
 def check(M, N, K_, cuda_device, out_dtype=torch.float16, cfg=None, seed=0, with_acc=True, sw_offset=0):
     """Dequantised output bit-exact against the oracle; with_acc also returns
     the raw int32 accumulators (which routes the tile kernels' epilogue
-    through per-row stores; without them 16-bit outputs go through the
-    staged epilogue).  sw_offset shifts sW by that many floats in its
+    through per-row stores; without them 16-bit and fp32 outputs go through
+    the staged epilogue).  sw_offset shifts sW by that many floats in its
     buffer (unaligned scales also take the per-row path)."""
     A, W, sA, sW = WL.int8_gemm_inputs(M, N, K_, device=cuda_device, seed=seed)
     if sw_offset:
@@ -36,10 +36,11 @@ def check(M, N, K_, cuda_device, out_dtype=torch.float16, cfg=None, seed=0, with
     assert torch.equal(C.cpu(), exp)
 
 
-# the staged epilogue (16-bit outputs, no raw accumulators): 128-column groups
-# staged in shared memory and written as whole row runs, ragged edges by rows
+# the staged epilogue (no raw accumulators): groups of 256-byte rows (128
+# columns of a 16-bit output, 64 of fp32) staged in shared memory and written
+# as whole row runs, ragged edges by rows
 @pytest.mark.parametrize("cfg", [None, {"tile_n": 128}, {"tile_n": 224}, {"flags": 2}, {"flags": 2, "tile_n": 128}])
-@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("M,N,K_", [(600, 1000, 640), (512, 4096, 1024), (300, 448, 256), (4096, 1280, 128)])
 def test_int8_gemm_staged_epilogue(cfg, out_dtype, M, N, K_, cuda_device):
     for seed in (0, 1):
@@ -54,11 +55,13 @@ def test_int8_gemm_staged_epilogue(cfg, out_dtype, M, N, K_, cuda_device):
 @pytest.mark.parametrize("with_acc", [True, False])
 def test_int8_gemm_last_wave_halves(cfg, M, N, K_, with_acc, cuda_device):
     check(M, N, K_, cuda_device, cfg=cfg, with_acc=with_acc)
+    if not with_acc:
+        check(M, N, K_, cuda_device, out_dtype=torch.float32, cfg=cfg, with_acc=False)
 
 
 def test_int8_gemm_unaligned_scales_take_the_row_path(cuda_device):
     check(600, 1000, 640, cuda_device, with_acc=False, sw_offset=1)
-    check(600, 1000, 640, cuda_device, out_dtype=torch.float32, with_acc=False)
+    check(600, 1000, 640, cuda_device, out_dtype=torch.float32, with_acc=False, sw_offset=1)
 
 
 @pytest.mark.parametrize("M,N,K_", [(128, 256, 128), (256, 512, 1024), (130, 200, 48), (1, 8, 16),

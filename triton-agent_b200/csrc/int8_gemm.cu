@@ -62,7 +62,7 @@ struct GemmParams {
   int64_t col_off;
   void* dst[kMaxRanks];
   const void* bias;     // bias + GELU flavour: [N] of the output type
-  int staged;           // tile kernels: 128-column groups through the staged epilogue (gather_group)
+  int staged;           // tile kernels: 256-byte row groups through the staged epilogue (gather_group)
   // CTA-pair kernel work items: items < full_items are whole tiles; the
   // last partial wave's tiles follow as two half-width items each
   int full_items, num_items;
@@ -161,9 +161,14 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* acc, int64_t row,
 // The next 32 columns' TMEM load is in flight while a chunk is dequantised,
 // and the group's 128 column scales are one 16-byte load per lane,
 // broadcast by shuffles.
-constexpr int kGatherCols = 128;
-constexpr int kGatherRowBytes = kGatherCols * 2 + 16;  // +16 B: conflict-free both ways
+constexpr int kGatherRowData = 256;                     // bytes of one row of a group
+constexpr int kGatherRowBytes = kGatherRowData + 16;     // +16 B: conflict-free both ways
 constexpr int kGatherWarpBytes = 32 * kGatherRowBytes;
+// columns of a staged group: 128 of a 16-bit output, 64 of fp32
+template <typename OutT>
+constexpr int gather_cols() {
+  return kGatherRowData / (int)sizeof(OutT);
+}
 
 // release: when non-zero, the address (shared::cluster) of the accumulator
 // buffer's empty barrier, arrived on as soon as this group's last TMEM load
@@ -174,18 +179,32 @@ __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int l
                                              const float* __restrict__ sA, const float* __restrict__ sW,
                                              OutT* __restrict__ C, const GemmParams& p, uint8_t* stage,
                                              uint32_t release = 0) {
-  static_assert(sizeof(OutT) == 2, "staged gather is for 16-bit outputs");
+  constexpr int GC = gather_cols<OutT>();
+  constexpr int VN = Vec<OutT>::N;  // outputs per 16-byte piece
   const int64_t row = row0 + lane;
   const float sa = row < p.M ? sA[row] : 0.f;
-  // scales of columns col0 + 4 lane .. col0 + 4 lane + 3 (col0 is 16-byte aligned in sW)
-  const float4 sw4 = __ldg(reinterpret_cast<const float4*>(sW + col0) + lane);
+  // scales: lane holds columns col0 + SW lane .. + SW - 1 (4 of 128 for 16-bit
+  // outputs, 2 of 64 for fp32), one aligned load, broadcast by shuffles
+  constexpr int SW = GC / 32;
+  float swv[SW];
+  if constexpr (SW == 4) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(sW + col0) + lane);
+    swv[0] = t.x;
+    swv[1] = t.y;
+    swv[2] = t.z;
+    swv[3] = t.w;
+  } else {
+    const float2 t = __ldg(reinterpret_cast<const float2*>(sW + col0) + lane);
+    swv[0] = t.x;
+    swv[1] = t.y;
+  }
   uint32_t acc[2][32];
   sm100::tmem_ld_32x32b_x32(t_row, acc[0]);
 #pragma unroll
-  for (int c4 = 0; c4 < kGatherCols / 32; ++c4) {
+  for (int c4 = 0; c4 < GC / 32; ++c4) {
     sm100::tmem_wait_ld_regs(acc[c4 & 1]);
-    if (c4 + 1 < kGatherCols / 32) sm100::tmem_ld_32x32b_x32(t_row + (c4 + 1) * 32, acc[(c4 + 1) & 1]);
-    if (c4 + 1 == kGatherCols / 32 && release != 0) {
+    if (c4 + 1 < GC / 32) sm100::tmem_ld_32x32b_x32(t_row + (c4 + 1) * 32, acc[(c4 + 1) & 1]);
+    if (c4 + 1 == GC / 32 && release != 0) {
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive_cluster(release);
@@ -193,13 +212,14 @@ __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int l
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      // column c4 * 32 + j: component j % 4 of lane c4 * 8 + j / 4
-      const float mine = (j & 3) == 0 ? sw4.x : (j & 3) == 1 ? sw4.y : (j & 3) == 2 ? sw4.z : sw4.w;
-      v[j] = dequant(acc[c4 & 1][j], sa, __shfl_sync(0xffffffffu, mine, c4 * 8 + (j >> 2)));
+      // column c4 * 32 + j: component j % SW of lane (c4 * 32 + j) / SW
+      v[j] = dequant(acc[c4 & 1][j], sa, __shfl_sync(0xffffffffu, swv[j % SW], (c4 * 32 + j) / SW));
     }
+    // 32 columns = 32 * sizeof(OutT) bytes of the staged row
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint4*>(stage + lane * kGatherRowBytes + c4 * 64 + q * 16) = pack16<OutT>(v + 8 * q);
+    for (int q = 0; q < 32 / VN; ++q)
+      *reinterpret_cast<uint4*>(stage + lane * kGatherRowBytes + c4 * 32 * (int)sizeof(OutT) + q * 16) =
+          pack16<OutT>(v + VN * q);
   }
   __syncwarp();
 #pragma unroll 4
@@ -208,7 +228,7 @@ __device__ __forceinline__ void gather_group(uint32_t t_row, int64_t row0, int l
     const uint4 w = *reinterpret_cast<const uint4*>(stage + r * kGatherRowBytes + piece * 16);
     const int64_t grow = row0 + r;
     if (grow < p.M) {
-      const int64_t off = grow * p.ldc + p.col_off + col0 + piece * 8;
+      const int64_t off = grow * p.ldc + p.col_off + col0 + piece * VN;
       *reinterpret_cast<uint4*>(C + off) = w;
       for (int k = 1; k < p.world; ++k) {
         int d = p.self + k;
@@ -439,11 +459,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN;) {
         const int64_t col0 = (int64_t)n_tile * BN + c;
-        if constexpr (sizeof(OutT) == 2) {
-          if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= BN) {  // warp-uniform
+        {
+          constexpr int GC = gather_cols<OutT>();
+          if (p.staged && col0 + GC <= p.N && c + GC <= BN) {  // warp-uniform
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes);
-            c += kGatherCols;
+            c += GC;
             continue;
           }
         }
@@ -644,17 +665,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const PairItem itm = pair_item(p, t, PN);
       const int64_t row = (int64_t)itm.m_tile * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
       const uint32_t t_row = tmem + a * PN + ((uint32_t)(quarter * 32) << 16);
-#pragma unroll 1
       bool released = false;
       for (int c = 0; c < itm.w;) {
         const int64_t col0 = itm.col + c;
-        if constexpr (sizeof(OutT) == 2 && !kF16) {
-          if (p.staged && col0 + kGatherCols <= p.N && c + kGatherCols <= itm.w) {  // warp-uniform
+        if constexpr (!kF16) {
+          constexpr int GC = gather_cols<OutT>();
+          if (p.staged && col0 + GC <= p.N && c + GC <= itm.w) {  // warp-uniform
             // the tile's last group hands the accumulator back before its rows go out
-            released = c + kGatherCols == itm.w;
+            released = c + GC == itm.w;
             gather_group<OutT>(t_row + c, row - lane, lane, col0, sA, sW, C, p,
                                bars.gather + (warp - 2) * kGatherWarpBytes, released ? acc_empty0 + a * 8 : 0u);
-            c += kGatherCols;
+            c += GC;
             continue;
           }
         }
@@ -1281,12 +1302,13 @@ int gemm_entry(const int8_t* A, const int8_t* W, const float* sA, const float* s
   if (ldc < N) return B200_ERR_BAD_ARG;
   if (!aligned16(A) || !aligned16(W)) return B200_ERR_ALIGNMENT;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return B200_ERR_UNSUPPORTED;
-  // Staged epilogue (16-bit outputs of the tile kernels, no raw accumulators,
-  // 16-byte aligned scales and output rows): 16 B alignment slack + one
+  // Staged epilogue (16-bit or fp32 outputs of the tile kernels, no raw
+  // accumulators, 16-byte aligned scales and output rows): 16 B alignment slack + one
   // staging buffer per epilogue warp.  The fused all-gather falls back to
   // per-row stores into every rank's C where these do not hold.
-  const bool staged = dtype_size(out_dtype) == 2 && acc_out == nullptr && aligned16(sW) &&
-                      aligned16(C) && (ldc * 2) % 16 == 0 && (ga.col_off * 2) % 16 == 0;
+  const int64_t osz = dtype_size(out_dtype);
+  const bool staged = (osz == 2 || osz == 4) && acc_out == nullptr && aligned16(sW) && aligned16(C) &&
+                      (ldc * osz) % 16 == 0 && (ga.col_off * osz) % 16 == 0;
   const GemmPlan g = plan_gemm(M, N, K, cfg, staged ? 16 + 4 * kGatherWarpBytes : 0);
   if (g.skinny && (g.splits > 1 || g.stream)) {
     if (workspace == nullptr || workspace_bytes < g.ws_bytes || !aligned16(workspace)) return B200_ERR_WORKSPACE;
