@@ -83,6 +83,13 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         gemm_ok = gemm_ok and bool(torch.equal(C2, full2)) and K.read_device_error(dev) == 0
         fused2.close()
+        # fp32 output through the fused all-gather (the staged epilogue's 64-column groups)
+        full32 = K.int8_gemm(A, W, sA, sW, out_dtype=torch.float32)
+        fused32 = FusedAllGatherGemm(M, N, out_dtype=torch.float32, device=dev)
+        C32 = fused32(A, W[n0:n1].contiguous(), sA, sW[n0:n1].contiguous())
+        torch.cuda.synchronize()
+        gemm_ok = gemm_ok and bool(torch.equal(C32, full32)) and K.read_device_error(dev) == 0
+        fused32.close()
         # batch-sharded decode: same inputs on every rank, each computes its share
         cache = WL.paged_cache(num_blocks=2048, block_size=16, Hkv=8, D=128, device=dev, seed=6)
         att = WL.decode_attention_inputs(cache, B=16, Hq=32, ctx_lo=100, ctx_hi=1500, device=dev, seed=6)
