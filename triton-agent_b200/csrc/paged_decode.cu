@@ -946,11 +946,13 @@ __global__ void __launch_bounds__(288, 1)
     }
   }
   __syncthreads();
-  // With programmatic dependent launch (cfg flags bit 3) everything above
-  // (contexts, entry prefix, barriers) overlaps the previous kernel's tail;
-  // nothing below may read q or a KV page before that grid has completed and
-  // its writes are visible.  A no-op for an ordinary launch.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // With programmatic dependent launch (cfg flags bit 3) everything up to
+  // each role's griddepcontrol.wait overlaps the previous kernel (whose
+  // caller guarantees it writes neither context_len nor block_table): the
+  // contexts, entry prefix and barriers above, and the producer's walk of
+  // the block table up to its first page copy.  No q, KV page or output
+  // byte is touched before the wait, after which that grid has completed
+  // and its writes are visible.  A no-op for an ordinary launch.
   const int64_t E = s_cum[p.nseg];
   const int64_t Gc = gridDim.x;
   FlatRanges R;
@@ -966,6 +968,7 @@ __global__ void __launch_bounds__(288, 1)
 
   // Segments without entries (context <= 0) are never streamed: zero them.
   if (warp < HG) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int s = c; s < p.nseg; s += (int)Gc) {
       if (s_cum[s + 1] != s_cum[s]) continue;
       const int64_t b = s % B, hg = s / B;
@@ -986,6 +989,7 @@ __global__ void __launch_bounds__(288, 1)
     const unsigned lt_mask = (1u << lane) - 1u;
     int it = 0;
     bool ok = true;
+    bool dep_waited = false;  // griddepcontrol.wait done by this lane
     // lane 0 pushes one ring entry; returns false on timeout
     auto push = [&](const PageMeta& m, int32_t tok0, int32_t h0) -> bool {
       const int st = it % p.stages;
@@ -993,6 +997,10 @@ __global__ void __launch_bounds__(288, 1)
       meta[st] = m;
       const uint32_t fb = sm100::smem_u32(&full_bar[st]);
       if (m.kind == 0) {
+        if (!dep_waited) {  // the first page copy waits for the previous kernel
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          dep_waited = true;
+        }
         sm100::mbar_arrive_expect_tx(fb, p.stage_bytes);
         const uint32_t dst = base + st * p.stage_bytes;
         sm100::tma_load_3d(dst, &tm_k, fb, 0, tok0, h0);
@@ -1169,7 +1177,11 @@ __global__ void __launch_bounds__(288, 1)
         if (s_flags[1]) {
           // ---- merge the segment's pieces (ranges c1..c2): per-head max and
           // 1/sum, then per-piece weights in shared memory and independent
-          // 16-byte loads of the pieces' o rows
+          // 16-byte loads of the pieces' o rows.  The merging CTA is one of
+          // the last to finish, so every step keeps its loads in flight
+          // together: a lane folds the (m, l) of its pieces for up to four heads
+          // of its warp at once into running (max, sum) pairs, combined over
+          // the warp by a butterfly.
           __threadfence();
           const int np = m.c2 - m.c1 + 1;
           auto piece = [&](int i, int hh) -> const float* {
@@ -1177,22 +1189,74 @@ __global__ void __launch_bounds__(288, 1)
             const int sl = (cc == m.c1) ? m.c1_slot : 0;
             return ws_rows + ((int64_t)(cc * 2 + sl) * heads_cta + hh) * kFlatPitch;
           };
-          for (int hh = w; hh < heads_cta; hh += HG) {
-            float mx = -INFINITY;
-            for (int i = lane; i < np; i += 32) mx = fmaxf(mx, __ldcg(piece(i, hh) + kD));
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            float L = 0.f;
-            for (int i = lane; i < np; i += 32) {
-              const float* r = piece(i, hh);
-              const float mc = __ldcg(r + kD);
-              L += (mc == -INFINITY) ? 0.f : exp2f(mc - mx) * __ldcg(r + kD + 1);
+          // (mx, L) += a piece (mc, lc): the sum rescaled to the larger max
+          auto fold = [](float& mx, float& L, float mc, float lc) {
+            if (mc == -INFINITY) return;
+            if (mc > mx) {
+              L = (mx == -INFINITY ? 0.f : L * exp2f(mx - mc)) + lc;
+              mx = mc;
+            } else {
+              L = fmaf(exp2f(mc - mx), lc, L);
             }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-            if (lane == 0) {
-              s_comb[hh] = mx;
-              s_comb[64 + hh] = L > 0.f ? 1.f / L : 0.f;
+          };
+          if constexpr (G <= 4) {
+            constexpr int GB = G < 4 ? G : 4;  // heads of the warp folded together
+  #pragma unroll
+            for (int kb = 0; kb < G; kb += GB) {
+              float mxh[GB], Lh[GB];
+  #pragma unroll
+              for (int k = 0; k < GB; ++k) {
+                mxh[k] = -INFINITY;
+                Lh[k] = 0.f;
+              }
+              for (int i = lane; i < np; i += 32) {
+                float mi[GB], li[GB];
+  #pragma unroll
+                for (int k = 0; k < GB; ++k) {
+                  const float* r = piece(i, w + (kb + k) * HG);
+                  mi[k] = __ldcg(r + kD);
+                  li[k] = __ldcg(r + kD + 1);
+                }
+  #pragma unroll
+                for (int k = 0; k < GB; ++k) fold(mxh[k], Lh[k], mi[k], li[k]);
+              }
+  #pragma unroll
+              for (int off = 16; off > 0; off >>= 1) {
+  #pragma unroll
+                for (int k = 0; k < GB; ++k) {
+                  const float om = __shfl_xor_sync(0xffffffffu, mxh[k], off);
+                  const float ol = __shfl_xor_sync(0xffffffffu, Lh[k], off);
+                  fold(mxh[k], Lh[k], om, ol);
+                }
+              }
+              if (lane == 0) {
+  #pragma unroll
+                for (int k = 0; k < GB; ++k) {
+                  s_comb[w + (kb + k) * HG] = mxh[k];
+                  s_comb[64 + w + (kb + k) * HG] = Lh[k] > 0.f ? 1.f / Lh[k] : 0.f;
+                }
+              }
+            }
+          } else {
+            // eight heads a warp: one head at a time (the folded form's
+            // registers spill here)
+            for (int hh = w; hh < heads_cta; hh += HG) {
+              float mx = -INFINITY;
+              for (int i = lane; i < np; i += 32) mx = fmaxf(mx, __ldcg(piece(i, hh) + kD));
+  #pragma unroll
+              for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+              float L = 0.f;
+              for (int i = lane; i < np; i += 32) {
+                const float* r = piece(i, hh);
+                const float mc = __ldcg(r + kD);
+                L += (mc == -INFINITY) ? 0.f : exp2f(mc - mx) * __ldcg(r + kD + 1);
+              }
+  #pragma unroll
+              for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+              if (lane == 0) {
+                s_comb[hh] = mx;
+                s_comb[64 + hh] = L > 0.f ? 1.f / L : 0.f;
+              }
             }
           }
           named_bar_sync(1, nthr);
